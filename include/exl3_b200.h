@@ -1,0 +1,132 @@
+/*
+ * exl3_b200.h -- C ABI of the B200 (sm_100a) EXL3 quantized-linear hot path.
+ *
+ * One shared library, libexl3b200.so, built from omlx_exl3_b200/csrc/. Plain pointers and sizes, no
+ * framework types: device buffers are owned by the caller, `stream` is a cudaStream_t passed as void*,
+ * and every entry point returns 0 (EXL3_OK) or a negative EXL3_E* status (exl3_strerror() names it).
+ * No entry point allocates device memory; scratch space is passed in by the caller.
+ *
+ * The reference (daig/omlx-exl3) has no C ABI: its kernels are Metal source JIT-compiled through MLX
+ * (src/omlx/exl3/kernels.py). Each entry point below names the reference function it replaces. The
+ * reference-side Python binding a maintainer would write is shown in INTEGRATION.md; the package
+ * omlx_exl3_b200 binds this header through ctypes the same way.
+ *
+ * Dtype codes: EXL3_F16 = 0, EXL3_BF16 = 1, EXL3_F32 = 2.
+ * Trellis buffers are the checkpoint's int16 [k/16][n/16][16K] tensors viewed as uint32 words and
+ * must be 16-byte aligned.
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EXL3_API __attribute__((visibility("default")))
+#else
+#define EXL3_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    EXL3_OK = 0,
+    EXL3_E_SHAPE = -1,      /* k, n, rows or member count out of range / not a multiple */
+    EXL3_E_BITS = -2,       /* bits per weight not in 1..8 */
+    EXL3_E_CODEBOOK = -3,   /* codebook not in 0..2 */
+    EXL3_E_DTYPE = -4,      /* unsupported dtype code */
+    EXL3_E_ALIGN = -5,      /* a pointer is not aligned as required */
+    EXL3_E_NULL = -6,       /* a required pointer is NULL */
+    EXL3_E_CUDA = -7,       /* a CUDA launch or attribute call failed */
+    EXL3_E_WORKSPACE = -8,  /* scratch buffer too small */
+    EXL3_E_DEVICE = -9      /* device is not sm_100 */
+};
+
+enum { EXL3_F16 = 0, EXL3_BF16 = 1, EXL3_F32 = 2 };
+
+/* Human-readable name of a status code. */
+EXL3_API const char* exl3_strerror(int status);
+
+/* ABI version, (major << 16) | minor. */
+EXL3_API int exl3_version(void);
+
+/*
+ * Trellis -> W^T decode, bit-exact fp16.
+ * Replaces: kernels.decode_wt (src/omlx/exl3/kernels.py:340-351).
+ * Writes columns [16*nt0, 16*(nt0+ntc)) of the k x n weight as an (16*ntc, k) row-major fp16
+ * matrix `w` (row = output feature). ntc < 0 means "to the end".
+ */
+EXL3_API int exl3_decode_wt(const uint32_t* trellis, int k, int n, int bits, int codebook, int nt0, int ntc,
+                   void* w, void* stream);
+
+/*
+ * Decode GEMV for 1..8 rows (decode / speculative verify), one launch for a linear or a sibling group.
+ * Replaces: kernels.TrellisGemvPlan.__call__ (src/omlx/exl3/kernels.py:263-299, kernel :114-209).
+ *   y[r, :] = concat_m( had128(xh[m, r, :] @ W_m) / sqrt(128) ) * svh      (y in out_dtype)
+ * xh: fp16 (n_members, rows, k); trellis[m]: member m's k x n[m] trellis; svh: fp16 (sum n);
+ * y: (rows, sum n) fp16 or bf16. All members share k, bits and codebook; each n[m] % 128 == 0.
+ * partials / counters: scratch from exl3_gemv_workspace(). `counters` must be zeroed once when it is
+ * allocated (exl3_gemv_reset); every completed call leaves it zeroed again. Calls that share one
+ * scratch buffer must not overlap on the GPU (use one scratch per stream).
+ */
+typedef struct exl3_gemv_desc {
+    int32_t k;           /* in_features, multiple of 16 */
+    int32_t n_members;   /* 1..3 */
+    int32_t n[3];        /* out_features of each member, multiples of 128 */
+    int32_t bits;        /* 1..8 */
+    int32_t codebook;    /* 0 = 3inst, 1 = mcg, 2 = mul1 */
+    int32_t rows;        /* 1..8 */
+    int32_t out_dtype;   /* EXL3_F16 or EXL3_BF16 */
+    int32_t grid;        /* CTAs to use; 0 = one per SM of the current device */
+    int32_t flags;       /* EXL3_GEMV_ROW_EXACT: row r's result does not depend on `rows` */
+} exl3_gemv_desc;
+
+/* exl3_gemv_desc.flags. Without ROW_EXACT a single row takes a CUDA-core path (half2 products,
+ * fp32 sums every 16 products) that is faster than the tensor-core path used for 2..8 rows; with it,
+ * one row also takes the tensor-core path, so row r of any call gives the same bits
+ * (the reference kernel's row-exact property, src/omlx/exl3/kernels.py:13-15). */
+enum { EXL3_GEMV_ROW_EXACT = 1 };
+
+EXL3_API int exl3_gemv_workspace(const exl3_gemv_desc* desc, size_t* partial_bytes, size_t* counter_bytes);
+EXL3_API int exl3_gemv_reset(uint32_t* counters, size_t counter_bytes, void* stream);
+EXL3_API int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
+              void* y, float* partials, uint32_t* counters, void* stream);
+
+/*
+ * Input rotation for 1..3 members: xh[m, r, :] = fp16( had128(x[r, :] * suh[m, :]) / sqrt(128) ).
+ * Replaces: kernels.rot (src/omlx/exl3/kernels.py:451-458). x: (rows, k) of x_dtype; suh: fp16
+ * (n_members, k); xh: fp16 (n_members, rows, k); k % 128 == 0.
+ */
+EXL3_API int exl3_rot(const void* x, int x_dtype, int rows, int k, const void* suh, int n_members, void* xh, void* stream);
+
+/*
+ * RMSNorm (MLX rounding: xn = T(w * T(x * rsqrt(mean(x^2) + eps)))) fused with the input rotation
+ * of every consumer. Replaces: kernels.norm_rot (src/omlx/exl3/kernels.py:461-473).
+ * x, w, xn: (rows, k) / (k) / (rows, k) of dtype (EXL3_F16 or EXL3_BF16); suh: fp16 (n_members, k);
+ * xh: fp16 (n_members, rows, k); k % 128 == 0.
+ */
+EXL3_API int exl3_norm_rot(const void* x, const void* w, int dtype, int rows, int k, float eps, const void* suh,
+                  int n_members, void* xn, void* xh, void* stream);
+
+/*
+ * SwiGLU fused with down_proj's input rotation: xh[r, :] = fp16(had128(silu(g) * u * suh) / sqrt(128))
+ * with gu = [g | u] (rows, 2n) of gu_dtype. Replaces: kernels.swiglu_rot (src/omlx/exl3/kernels.py:476-483).
+ * suh: fp16 (n); xh: fp16 (1, rows, n); n % 128 == 0.
+ */
+EXL3_API int exl3_swiglu_rot(const void* gu, int gu_dtype, int rows, int n, const void* suh, void* xh, void* stream);
+
+/*
+ * Output rotation: out[r, :] = out_dtype(had128(y[r, :]) / sqrt(128) * svh), y (rows, n) of y_dtype.
+ * Replaces: the prefill tail `_had128(y) * self._svh` (src/omlx/exl3/linear.py:105, :31-33).
+ * svh: fp16 (n); n % 128 == 0.
+ */
+EXL3_API int exl3_had_svh(const void* y, int y_dtype, int rows, int n, const void* svh, void* out, int out_dtype,
+                          void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3_B200_H */

@@ -1,0 +1,370 @@
+// EXL3 (ExLlamaV3 trellis) decode primitives for sm_100a.
+//
+// Weight format (daig/omlx-exl3 src/omlx/exl3/kernels.py:4-8): a K-bit tensor of shape k x n is
+// stored as int16 trellis[k/16][n/16][16K]. Each 16x16 tile is a tail-biting bitstream of 256*K
+// bits held as 8K little-endian uint32 words, bits read MSB-first. The 16-bit state of stream
+// position t (0..255) is bits [(t+1)K - 16, (t+1)K) of the stream, modulo 256K. Run g (0..7) is
+// positions 32g..32g+31; position p of a run holds tile column g + 8*[(p%8) >= 4] and tile k-row
+// 2*(p/8) + (p%2) + 8*[(p%4) >= 2] (kernels.py:52-55).
+//
+// Those eight consecutive positions 8L..8L+7 of lane L = 4g + q are exactly the eight weights
+// that lane L holds in the A fragment of an m16n8k16 MMA whose rows are the tile's 16 output
+// columns and whose k is the tile's 16 k-rows: (row g | g+8) x (k 2q, 2q+1, 2q+8, 2q+9). So one
+// warp decodes one tile straight into MMA fragments, each lane from one small bit window.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace exl3 {
+
+// ------------------------------------------------------------------------------ codebooks
+// 16-bit state -> weight (kernels.py:26-48). cb 0 "3inst", 1 "mcg", 2 "mul1".
+constexpr uint32_t k3instMul = 89226354u, k3instAdd = 64248484u;
+constexpr uint32_t kMcgMul = 0xCBAC1FEDu;
+constexpr uint32_t kMul1Mul = 0x83DCD12Du;
+constexpr uint16_t kMul1InvBits = 0x1eee, kMul1BiasBits = 0xc931;   // fp16 1/K and bias
+
+// The raw pair of fp16 halves whose sum is the 3inst / mcg weight.
+template <int CB>
+__device__ __forceinline__ uint32_t hash_pair(uint32_t s)
+{
+    const uint32_t h = CB == 0 ? s * k3instMul + k3instAdd : s * kMcgMul;
+    return (h & 0x8fff8fffu) ^ 0x3b603b60u;
+}
+
+// mul1: fp16 bits of 1024 + (sum of the 4 bytes of the hash), in the low half (high half 0).
+__device__ __forceinline__ uint32_t mul1_r(uint32_t s)
+{
+    return __dp4a(s * kMul1Mul, 0x01010101u, 0x6400u);
+}
+
+// Bit-exact fp16 weight of one state (the reference's dec1<CB>): one fp16 add or one fp16 fma.
+template <int CB>
+__device__ __forceinline__ __half dec1(uint32_t s)
+{
+    if constexpr (CB == 2) {
+        const __half r = __ushort_as_half((unsigned short)mul1_r(s));
+        return __hfma(r, __ushort_as_half(kMul1InvBits), __ushort_as_half(kMul1BiasBits));
+    } else {
+        const uint32_t v = hash_pair<CB>(s);
+        return __hadd(__ushort_as_half((unsigned short)(v & 0xffffu)), __ushort_as_half((unsigned short)(v >> 16)));
+    }
+}
+
+// MMA A-operand word for one state in the "split" form used by the GEMV: a half2 (a, b) whose
+// a*x + b*x equals the weight times x. For 3inst / mcg that is the hash pair itself (the weight
+// is the sum of its halves, here left unrounded); for mul1 it is (fma(r, 1/K, bias), 0).
+template <int CB>
+__device__ __forceinline__ uint32_t split_word(uint32_t s)
+{
+    if constexpr (CB == 2) {
+        const __half2 r = __halves2half2(__ushort_as_half((unsigned short)mul1_r(s)), __ushort_as_half(0));
+        const __half2 a = __halves2half2(__ushort_as_half(kMul1InvBits), __ushort_as_half(0));
+        const __half2 c = __halves2half2(__ushort_as_half(kMul1BiasBits), __ushort_as_half(0));
+        const __half2 w = __hfma2(r, a, c);
+        return *reinterpret_cast<const uint32_t*>(&w);
+    } else {
+        return hash_pair<CB>(s);
+    }
+}
+
+// ------------------------------------------------------------------------------ bit windows
+// Lane L's positions 8L..8L+7 end at stream bit E = 8K(L+1). Let V be the stream bits just before
+// E read as a number whose bit i is stream bit E-1-i. The state of the lane's j-th position is then
+// (V >> (7-j)K) & 0xffff. V needs 7K+16 bits: one word (K <= 2), two (K <= 6) or three (K >= 7).
+template <int K>
+struct LaneWindow {
+    static constexpr int TW = 8 * K;                     // words per tile
+    static constexpr int NEED = 7 * K + 16;              // bits of V used
+    static constexpr bool kAligned = (K % 4) == 0;       // E is a multiple of 32: no shift
+    int idx[4];                                          // word indices (mod TW), latest first
+    uint32_t shift;                                      // right shift that puts bit E-1 at bit 0
+
+    __device__ __forceinline__ explicit LaneWindow(int lane)
+    {
+        const int E = 8 * K * (lane + 1);
+        const int iw = (E - 1) >> 5;
+        shift = kAligned ? 0u : (uint32_t)((32 * (iw + 1) - E) & 31);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) idx[q] = ((iw - q) % TW + TW) % TW;
+    }
+};
+
+// V as three 32-bit words (bits [0,32), [32,64), [64,96)) from the tile's words.
+template <int K>
+struct Window96 {
+    uint32_t lo, mid, hi;
+};
+
+template <int K>
+__device__ __forceinline__ Window96<K> load_window(const uint32_t* tile, const LaneWindow<K>& lw)
+{
+    constexpr int NEED = LaneWindow<K>::NEED;
+    constexpr bool A = LaneWindow<K>::kAligned;
+    Window96<K> v;
+    const uint32_t w0 = tile[lw.idx[0]];
+    uint32_t w1 = 0, w2 = 0, w3 = 0;
+    if (!A || NEED > 32) w1 = tile[lw.idx[1]];
+    if (NEED > 32 && (!A || NEED > 64)) w2 = tile[lw.idx[2]];
+    if (NEED > 64 && !A) w3 = tile[lw.idx[3]];
+    if constexpr (A) {
+        v.lo = w0; v.mid = w1; v.hi = w2;
+    } else {
+        v.lo = __funnelshift_r(w0, w1, lw.shift);
+        v.mid = NEED > 32 ? __funnelshift_r(w1, w2, lw.shift) : 0u;
+        v.hi = NEED > 64 ? __funnelshift_r(w2, w3, lw.shift) : 0u;
+    }
+    return v;
+}
+
+// State of the lane's position j (0..7).
+template <int K, int J>
+__device__ __forceinline__ uint32_t lane_state(const Window96<K>& v)
+{
+    constexpr int sh = (7 - J) * K;
+    if constexpr (sh + 16 <= 32) {
+        return sh == 16 ? (v.lo >> 16) : ((v.lo >> sh) & 0xffffu);
+    } else if constexpr (sh < 32) {
+        return __funnelshift_r(v.lo, v.mid, sh) & 0xffffu;
+    } else if constexpr (sh + 16 <= 64) {
+        return sh == 48 ? (v.mid >> 16) : ((v.mid >> (sh - 32)) & 0xffffu);
+    } else if constexpr (sh < 64) {
+        return __funnelshift_r(v.mid, v.hi, sh - 32) & 0xffffu;
+    } else {
+        return (v.hi >> (sh - 64)) & 0xffffu;
+    }
+}
+
+// ------------------------------------------------------------------------------ balanced hashing
+// The decode is bound by two SM pipes: the integer ALU pipe (shifts, masks, byte permutes, the
+// codebook's and/xor) and the FMA pipe (integer multiply-adds), each 16 lanes per scheduler per
+// cycle. hashes8() produces the eight raw codebook hashes h_j = s_j * mul + add of a lane with
+// the state extractions split between the two pipes:
+//   exact    a 16-bit window isolated with a one-op form where one exists (and 0xffff, a byte
+//            permute, a multiply-high for the ">> 16"), else shift + mask;
+//   junk     X = any 32-bit value whose low half is the state and J = X >> 16; then
+//            s * mul + add = X * mul + add - J * (mul << 16), all on the FMA pipe. J is another
+//            state of the same lane when 16 is a multiple of K, else one multiply-high.
+__device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) { return __umulhi(a, b); }
+
+template <int SH>
+__device__ __forceinline__ uint32_t state_exact(const uint32_t (&w)[3])
+{
+    constexpr int wi = SH / 32, o = SH % 32;
+    if constexpr (o == 0) {
+        return w[wi] & 0xffffu;
+    } else if constexpr (o == 16) {
+        return mulhi(w[wi], 1u << 16);
+    } else if constexpr (o == 8) {
+        return __byte_perm(w[wi], 0u, 0x4421);
+    } else if constexpr (o + 16 <= 32) {
+        return mulhi(w[wi], 1u << (32 - o)) & 0xffffu;
+    } else {
+        return __funnelshift_r(w[wi], w[wi + 1], o) & 0xffffu;
+    }
+}
+
+// A 32-bit value whose low 16 bits are the state at SH. STREAM: its upper 16 bits must be the
+// following stream bits (the junk is then another state of the lane); otherwise any upper bits
+// do, and an in-word window is taken with a multiply-high on the FMA pipe.
+template <int SH, bool STREAM>
+__device__ __forceinline__ uint32_t state_loose(const uint32_t (&w)[3])
+{
+    constexpr int wi = SH / 32, o = SH % 32;
+    if constexpr (o == 0) return w[wi];
+    else if constexpr (!STREAM && o + 16 <= 32) return mulhi(w[wi], 1u << (32 - o));
+    else return __funnelshift_r(w[wi], w[wi + 1], o);
+}
+
+template <int CB>
+struct HashConst {
+    static constexpr uint32_t mul = CB == 0 ? k3instMul : (CB == 1 ? kMcgMul : kMul1Mul);
+    static constexpr uint32_t add = CB == 0 ? k3instAdd : 0u;
+    static constexpr uint32_t corr = 0u - (mul << 16);   // -(mul * 2^16) mod 2^32
+};
+
+// Which of the 8 states go through the junk form (bit j set), per bitrate. Chosen so that the
+// ALU and FMA instruction counts of a tile come out about equal (see the calibration notes in the
+// design document); the other states are extracted exactly.
+template <int K>
+struct JunkPlan {
+    static constexpr unsigned mask = K == 4 ? 0x80u : K == 8 ? 0x98u : K == 7 ? 0x60u : K == 6 ? 0x60u
+                                     : K == 5 ? 0x60u : K == 3 ? 0x30u : 0x00u;
+};
+
+template <int K, int CB>
+__device__ __forceinline__ void hashes8(const uint32_t (&w)[3], uint32_t (&h)[8])
+{
+    using C = HashConst<CB>;
+    constexpr unsigned JM = JunkPlan<K>::mask;
+    uint32_t s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = 0;
+    // exact states first (they may serve as the junk of later states)
+#define EXL3_EXACT(J)                                                     \
+    if constexpr (!(JM & (1u << J))) s[J] = state_exact<(7 - J) * K>(w);
+    EXL3_EXACT(0) EXL3_EXACT(1) EXL3_EXACT(2) EXL3_EXACT(3)
+    EXL3_EXACT(4) EXL3_EXACT(5) EXL3_EXACT(6) EXL3_EXACT(7)
+#undef EXL3_EXACT
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (!(JM & (1u << j))) h[j] = s[j] * C::mul + C::add;
+#define EXL3_JUNK(J)                                                                            \
+    if constexpr (JM & (1u << J)) {                                                             \
+        constexpr int SH = (7 - J) * K;                                                         \
+        constexpr bool kFromState = 16 % K == 0 && J >= 16 / K && !(JM & (1u << (J - 16 / K))); \
+        const uint32_t X = state_loose<SH, kFromState>(w);                                      \
+        uint32_t Jv;                                                                            \
+        if constexpr (kFromState) Jv = s[(J - 16 / K) & 7];                                     \
+        else Jv = mulhi(X, 1u << 16);                                                           \
+        h[J] = X * C::mul + C::add + Jv * C::corr;                                              \
+    }
+    EXL3_JUNK(0) EXL3_JUNK(1) EXL3_JUNK(2) EXL3_JUNK(3)
+    EXL3_JUNK(4) EXL3_JUNK(5) EXL3_JUNK(6) EXL3_JUNK(7)
+#undef EXL3_JUNK
+}
+
+// hash -> split MMA word (see split_word)
+template <int CB>
+__device__ __forceinline__ uint32_t split_from_hash(uint32_t h)
+{
+    if constexpr (CB == 2) {
+        const uint32_t r = __dp4a(h, 0x01010101u, 0x6400u);
+        const __half2 rr = *reinterpret_cast<const __half2*>(&r);
+        const __half2 a = __halves2half2(__ushort_as_half(kMul1InvBits), __ushort_as_half(0));
+        const __half2 c = __halves2half2(__ushort_as_half(kMul1BiasBits), __ushort_as_half(0));
+        const __half2 w = __hfma2(rr, a, c);
+        return *reinterpret_cast<const uint32_t*>(&w);
+    } else {
+        return (h & 0x8fff8fffu) ^ 0x3b603b60u;
+    }
+}
+
+// The lane's three window words (V bits [0,32), [32,64), [64,96)) of one tile.
+template <int K>
+__device__ __forceinline__ void window_words(const uint32_t* tile, const LaneWindow<K>& lw, uint32_t (&w)[3])
+{
+    const Window96<K> v = load_window<K>(tile, lw);
+    w[0] = v.lo;
+    w[1] = v.mid;
+    w[2] = v.hi;
+}
+
+// ------------------------------------------------------------------------------ MMA
+// D += A(16x16 fp16, row) * B(16x8 fp16, col), fp32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// ------------------------------------------------------------------------------ mbarrier / bulk copy
+__device__ __forceinline__ uint32_t smem_addr(const void* p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait: gives up (returns false) once `limit_ns` of wall time has passed without the phase
+// completing, so a lost completion turns into an error status instead of a hung GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && global_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// Global -> shared bulk copy (no multicast), completion counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 16-byte global -> shared copy through L2 only (LDGSTS), tracked by per-thread commit groups.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------------------------------ misc
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+constexpr float kHadScale = 0.08838834764831845f;   // 1/sqrt(128)
+
+// Error bits written to a caller-visible status word when a bounded wait gives up.
+enum : uint32_t { kStatusPipeTimeout = 1u, kStatusArrivalTimeout = 2u };
+
+}  // namespace exl3

@@ -1,0 +1,468 @@
+// EXL3 decode GEMV (1..8 rows) for sm_100a: y = had128(xh @ W) / sqrt(128) * svh in one launch.
+//
+// Replaces the reference's trellis GEMV (daig/omlx-exl3 src/omlx/exl3/kernels.py:114-299).
+//
+// Work split (stream-K over "units"): a unit is one 16-row k-slice of one 128-column output block,
+// i.e. 8 consecutive trellis tiles = 256*K contiguous bytes. Units are numbered block-major
+// (u = block * KT + kt) and each persistent CTA (one per SM) owns the contiguous range
+// [c*U/G, (c+1)*U/G), so every SM streams the same number of bytes whatever the shape.
+//
+// Inside a CTA every warp streams its own units (CTA unit indices w, w + NCW, ...) into a private
+// shared-memory ring with 16-byte cp.async copies, DEPTH - 1 units ahead of the unit it decodes (no
+// producer thread and no cross-warp handshake: many small copies from all warps keep enough bytes in
+// flight). A warp decodes each of the unit's 8 tiles straight into m16n8k16 A fragments (one lane =
+// 8 consecutive stream positions, exl3_common.cuh) and, for 2..8 rows, issues two MMAs per tile
+// against the rows of xh duplicated across each k pair ("split" operands: the 3inst/mcg weight is
+// the sum of two fp16 halves, so A = (lo, hi) and B = (x, x)); accumulators are fp32 registers.
+// For one row the same split words are multiplied on the CUDA cores instead (half2 FMA against
+// (x, x), flushed to fp32 every few units), which avoids the legacy MMA issue limit.
+//
+// Reduction, fixed order (bitwise reproducible, row-exact): at the end of each block segment the
+// consumer warps sum their accumulators through shared memory in warp order. A block that lies
+// entirely inside one CTA is finished right there; otherwise each CTA publishes its partial, and
+// the last CTA to arrive (per-block arrival counter, zero at rest) sums the partials in CTA order.
+// The finishing CTA applies the 128-point FWHT (Sylvester order, stages 1..64 as the reference),
+// * 1/sqrt(128) * svh, and writes y in the output dtype. No CTA ever waits on another CTA.
+#include <cuda_runtime.h>
+
+#include "exl3_b200.h"
+#include "exl3_common.cuh"
+#include "exl3_host.h"
+
+namespace exl3 {
+
+struct GemvParams {
+    const uint32_t* trellis[3];
+    int nt_member[3];        // n-tiles of each member (row stride of its trellis, in tiles)
+    int blk_off[4];          // first global 128-column block of each member; [nm] = total blocks
+    int nm;
+    const __half* xh;        // (nm, rows, k)
+    const __half* svh;       // (n_total)
+    void* y;                 // (rows, n_total)
+    float* partials;         // grid * J * 8 * 128
+    uint32_t* counters;      // blocks, then one status word
+    int k, KT, rows, n_total, blocks, out_bf16, J, row_exact;
+    long long units;
+};
+
+constexpr int kRedStride = 8 * 128;   // floats per warp partial (8 rows x 128 columns)
+// rows == 1: the half2 accumulators take kFlush units (4 products per half each) before they are
+// added into fp32, which bounds the fp16 accumulation to 16 products
+constexpr int kFlush = 4;
+
+template <int K, int NCW>
+struct GemvShape {
+    static constexpr int TW = 8 * K;                 // words per tile
+    static constexpr int UW = 8 * TW;                // words per unit (8 tiles)
+    static constexpr int UB = UW * 4;                // bytes per unit
+    static constexpr int D0 = (96 * 1024) / (NCW * UB);
+    static constexpr int DEPTH = D0 < 3 ? 3 : (D0 > 8 ? 8 : D0);   // units in flight per warp
+    static constexpr int RING = NCW * DEPTH * UB;
+    static constexpr int RED = NCW * kRedStride * 4;
+    static constexpr int SMEM = RING + RED;
+    static constexpr int THREADS = 32 * NCW;
+};
+
+__device__ __forceinline__ int owner_cta(long long u, long long U, int G)
+{
+    return (int)(((u + 1) * (long long)G - 1) / U);
+}
+
+__device__ __forceinline__ long long cta_start(int c, long long U, int G)
+{
+    return (long long)c * U / G;
+}
+
+// 128-point FWHT of one row held by one warp as v[i] = column lane + 32 i, then scale, svh, store.
+template <typename OT>
+__device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half* svh, OT* yrow)
+{
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[i], h);
+            v[i] = (lane & h) ? p - v[i] : v[i] + p;
+        }
+    }
+    {   // h = 32: columns c, c + 32 are v[i], v[i + 1] for i even
+        float a0 = v[0], a1 = v[1];
+        v[0] = a0 + a1; v[1] = a0 - a1;
+        a0 = v[2]; a1 = v[3];
+        v[2] = a0 + a1; v[3] = a0 - a1;
+    }
+    {   // h = 64
+        float a0 = v[0], a1 = v[2];
+        v[0] = a0 + a1; v[2] = a0 - a1;
+        a0 = v[1]; a1 = v[3];
+        v[1] = a0 + a1; v[3] = a0 - a1;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int c = lane + 32 * i;
+        yrow[c] = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
+    }
+}
+
+template <int K, int CB, int NCW, bool ROWS1>
+__global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
+{
+    using S = GemvShape<K, NCW>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    float* red = reinterpret_cast<float*>(smem + S::RING);
+    __shared__ int s_last;
+
+    const int lane = threadIdx.x & 31;
+    const int cw = threadIdx.x >> 5;
+    const int ctid = threadIdx.x;
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long U = p.units;
+    const long long u0 = cta_start(c, U, G), u1 = cta_start(c + 1, U, G);
+    const int n_units = (int)(u1 - u0);
+    const int KT = p.KT;
+
+    // Every warp streams its own units (CTA unit indices cw, cw + NCW, ...) into a private ring of
+    // DEPTH slots with 16-byte cp.async copies, DEPTH - 1 units ahead of the one it decodes.
+    uint32_t* wring = reinterpret_cast<uint32_t*>(smem) + (size_t)cw * S::DEPTH * S::UW;
+    int fi = cw;                                              // next unit index to fetch
+    int fb = (int)((u0 + fi) / KT), fkt = (int)(u0 + fi - (long long)fb * KT);
+    int fslot = 0;
+    auto fetch = [&]() {
+        if (fi < n_units) {
+            const int m = (p.nm > 1 && fb >= p.blk_off[1]) ? ((p.nm > 2 && fb >= p.blk_off[2]) ? 2 : 1) : 0;
+            const uint32_t* src = p.trellis[m] +
+                                  ((size_t)fkt * p.nt_member[m] + (size_t)(fb - p.blk_off[m]) * 8) * S::TW;
+            uint32_t* dst = wring + (size_t)fslot * S::UW;
+#pragma unroll
+            for (int cidx = lane; cidx < S::UB / 16; cidx += 32)
+                cp_async16(dst + cidx * 4, src + cidx * 4);
+            fi += NCW;
+            fkt += NCW;
+            while (fkt >= KT) { fkt -= KT; ++fb; }
+        }
+        cp_async_commit();                                    // (possibly empty) group per unit
+        fslot = fslot + 1 == S::DEPTH ? 0 : fslot + 1;
+    };
+#pragma unroll 1
+    for (int d = 0; d < S::DEPTH - 1; ++d) fetch();
+    int cslot = 0;                                            // ring slot of the unit being decoded
+
+    const int g = lane >> 2, q = lane & 3;
+    const LaneWindow<K> lw(lane);
+    const int rows = p.rows;
+    const int b_first = (int)(u0 / KT), b_last = (int)((u1 - 1) / KT);
+    const bool xlane = ROWS1 || g < rows;         // this lane carries a row of xh
+
+    for (int b = b_first; b <= b_last; ++b) {
+        const int m = (p.nm > 1 && b >= p.blk_off[1]) ? ((p.nm > 2 && b >= p.blk_off[2]) ? 2 : 1) : 0;
+        const __half* xrow = p.xh + ((size_t)m * rows + (ROWS1 ? 0 : g)) * p.k;
+        const int sa = (int)(max(u0, (long long)b * KT) - u0);
+        const int se = (int)(min(u1, (long long)(b + 1) * KT) - u0);
+
+        // MMA path: acc[j] = the m16n8 accumulator of tile j. rows == 1 path: acc[j][0] / [1] are
+        // columns g / g+8 of tile j in fp32, fed from half2 accumulators hacc every kFlush units.
+        float acc[8][4];
+        __half2 hacc[8][2];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+            hacc[j][0] = hacc[j][1] = __float2half2_rn(0.f);
+        }
+        int since_flush = 0;
+
+        const int kt_base = (int)(u0 - (long long)b * KT);     // k-slice of unit index 0 (may be < 0)
+        int i = sa + ((cw - sa) % NCW + NCW) % NCW;
+        // the lane's xh values for the next unit are fetched one unit ahead
+        uint32_t x0n = 0, x1n = 0;
+        if (i < se && xlane) {
+            const __half* xp = xrow + (kt_base + i) * 16 + 2 * q;
+            x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
+            x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
+        }
+        for (; i < se; i += NCW) {
+            const uint32_t x0 = x0n, x1 = x1n;
+            if (i + NCW < se && xlane) {
+                const __half* xp = xrow + (kt_base + i + NCW) * 16 + 2 * q;
+                x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
+                x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
+            }
+            // x duplicated across each k pair: (x[2q], x[2q]), (x[2q+8], ..), (x[2q+1], ..), (x[2q+9], ..)
+            const uint32_t be0 = prmt(x0, x0, 0x1010), be1 = prmt(x1, x1, 0x1010);
+            const uint32_t bo0 = prmt(x0, x0, 0x3232), bo1 = prmt(x1, x1, 0x3232);
+            fetch();                                  // unit + DEPTH - 1 (or an empty group)
+            cp_async_wait<S::DEPTH - 1>();            // this unit's copies have landed
+            __syncwarp();
+            const uint32_t* unit = wring + (size_t)cslot * S::UW;
+            cslot = cslot + 1 == S::DEPTH ? 0 : cslot + 1;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t w[3], h[8], a[8];
+                window_words<K>(unit + j * S::TW, lw, w);
+                hashes8<K, CB>(w, h);
+#pragma unroll
+                for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t]);
+                if constexpr (ROWS1) {
+                    // columns g (positions 0..3) and g+8 (4..7); k 2q, 2q+1, 2q+8, 2q+9
+                    const __half2 xe0 = *reinterpret_cast<const __half2*>(&be0);
+                    const __half2 xo0 = *reinterpret_cast<const __half2*>(&bo0);
+                    const __half2 xe1 = *reinterpret_cast<const __half2*>(&be1);
+                    const __half2 xo1 = *reinterpret_cast<const __half2*>(&bo1);
+                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[0]), xe0, hacc[j][0]);
+                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[1]), xo0, hacc[j][0]);
+                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[2]), xe1, hacc[j][0]);
+                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[3]), xo1, hacc[j][0]);
+                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[4]), xe0, hacc[j][1]);
+                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[5]), xo0, hacc[j][1]);
+                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[6]), xe1, hacc[j][1]);
+                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[7]), xo1, hacc[j][1]);
+                } else {
+                    // even k of the tile: (g,2q) (g+8,2q) (g,2q+8) (g+8,2q+8); odd k: the +1 neighbours
+                    mma16816(acc[j], a[0], a[4], a[2], a[6], be0, be1);
+                    mma16816(acc[j], a[1], a[5], a[3], a[7], bo0, bo1);
+                }
+            }
+            __syncwarp();                             // the slot is refilled by the next fetch
+            if constexpr (ROWS1) {
+                if (++since_flush == kFlush) {
+                    since_flush = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const float2 f = __half22float2(hacc[j][cc]);
+                            acc[j][cc] += f.x + f.y;
+                            hacc[j][cc] = __float2half2_rn(0.f);
+                        }
+                }
+            }
+        }
+
+        // ---- segment end: warp partials -> shared memory, summed in warp order
+        float* rw = red + cw * kRedStride;
+        if constexpr (ROWS1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const float2 f = __half22float2(hacc[j][cc]);
+                    float v = acc[j][cc] + (f.x + f.y);
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);     // the 4 lanes of column g
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    if (q == 0) rw[16 * j + g + 8 * cc] = v;
+                }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int col = 16 * j + g;
+                if (2 * q < rows) {
+                    rw[(2 * q) * 128 + col] = acc[j][0];
+                    rw[(2 * q) * 128 + col + 8] = acc[j][2];
+                }
+                if (2 * q + 1 < rows) {
+                    rw[(2 * q + 1) * 128 + col] = acc[j][1];
+                    rw[(2 * q + 1) * 128 + col + 8] = acc[j][3];
+                }
+            }
+        }
+        __syncthreads();
+        for (int e = ctid; e < rows * 128; e += 32 * NCW) {
+            float v = red[e];
+#pragma unroll
+            for (int w = 1; w < NCW; ++w) v += red[w * kRedStride + e];
+            red[e] = v;
+        }
+        __syncthreads();
+
+        const bool whole = (long long)b * KT >= u0 && (long long)(b + 1) * KT <= u1;
+        bool finish = whole;
+        if (!whole) {
+            // one warp publishes the CTA's partial and takes the block's arrival ticket
+            if (cw == 0) {
+                float* gp = p.partials + ((size_t)c * p.J + (b - b_first)) * kRedStride;
+                for (int e = lane; e < rows * 128; e += 32) gp[e] = red[e];
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) {
+                    const int c_first = owner_cta((long long)b * KT, U, G);
+                    const int c_last = owner_cta((long long)(b + 1) * KT - 1, U, G);
+                    const unsigned old = atomicAdd(&p.counters[b], 1u);
+                    const int last = old == (unsigned)(c_last - c_first);
+                    if (last) __threadfence();
+                    s_last = last;
+                }
+            }
+            __syncthreads();
+            finish = s_last != 0;
+            if (finish) {
+                const int c_first = owner_cta((long long)b * KT, U, G);
+                const int c_last = owner_cta((long long)(b + 1) * KT - 1, U, G);
+                for (int e = ctid; e < rows * 128; e += 32 * NCW) {
+                    float v = 0.f;
+                    for (int cc = c_first; cc <= c_last; ++cc) {
+                        const int jj = cc == c_first ? b - (int)(cta_start(cc, U, G) / KT) : 0;
+                        v += __ldcg(p.partials + ((size_t)cc * p.J + jj) * kRedStride + e);
+                    }
+                    red[e] = v;
+                }
+                if (ctid == 0) atomicExch(&p.counters[b], 0u);
+                __syncthreads();
+            }
+        }
+        if (finish) {
+            for (int r = cw; r < rows; r += NCW) {
+                float v[4];
+#pragma unroll
+                for (int ii = 0; ii < 4; ++ii) v[ii] = red[r * 128 + lane + 32 * ii];
+                const __half* sv = p.svh + (size_t)b * 128;
+                const size_t yoff = (size_t)r * p.n_total + (size_t)b * 128;
+                if (p.out_bf16)
+                    finish_row(v, lane, sv, reinterpret_cast<__nv_bfloat16*>(p.y) + yoff);
+                else
+                    finish_row(v, lane, sv, reinterpret_cast<__half*>(p.y) + yoff);
+            }
+        }
+        __syncthreads();   // red is reused by the next segment
+    }
+}
+
+// ---------------------------------------------------------------------------------------- host
+
+constexpr int kNCW = 16;
+
+struct GemvLaunch {
+    int grid, J, blocks, KT;
+    long long units;
+};
+
+static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
+{
+    if (!d) return EXL3_E_NULL;
+    if (d->k <= 0 || d->k % 16 || d->n_members < 1 || d->n_members > 3 || d->rows < 1 || d->rows > 8)
+        return EXL3_E_SHAPE;
+    if (d->bits < 1 || d->bits > 8) return EXL3_E_BITS;
+    if (d->codebook < 0 || d->codebook > 2) return EXL3_E_CODEBOOK;
+    if (d->out_dtype != EXL3_F16 && d->out_dtype != EXL3_BF16) return EXL3_E_DTYPE;
+    int blocks = 0;
+    for (int m = 0; m < d->n_members; ++m) {
+        if (d->n[m] <= 0 || d->n[m] % 128) return EXL3_E_SHAPE;
+        blocks += d->n[m] / 128;
+    }
+    L->blocks = blocks;
+    L->KT = d->k / 16;
+    L->units = (long long)blocks * L->KT;
+    long long G = d->grid > 0 ? d->grid : device_sm_count();
+    if (G > L->units) G = L->units;
+    L->grid = (int)G;
+    const long long per = (L->units + G - 1) / G;
+    L->J = (int)((per + L->KT - 1) / L->KT + 1);
+    return EXL3_OK;
+}
+
+template <int K, int CB, bool ROWS1>
+static int launch_gemv_v(const GemvParams& prm, int grid, cudaStream_t s)
+{
+    using S = GemvShape<K, kNCW>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(gemv_kernel<K, CB, kNCW, ROWS1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 S::SMEM) != cudaSuccess)
+            return EXL3_E_CUDA;
+        attr_set[dev] = true;
+    }
+    gemv_kernel<K, CB, kNCW, ROWS1><<<grid, S::THREADS, S::SMEM, s>>>(prm);
+    return launch_status();
+}
+
+template <int K, int CB>
+static int launch_gemv_k(const GemvParams& prm, int grid, cudaStream_t s)
+{
+    return prm.rows == 1 && !prm.row_exact ? launch_gemv_v<K, CB, true>(prm, grid, s)
+                                           : launch_gemv_v<K, CB, false>(prm, grid, s);
+}
+
+template <int K>
+static int launch_gemv_cb(int cb, const GemvParams& prm, int grid, cudaStream_t s)
+{
+    switch (cb) {
+    case 0: return launch_gemv_k<K, 0>(prm, grid, s);
+    case 1: return launch_gemv_k<K, 1>(prm, grid, s);
+    default: return launch_gemv_k<K, 2>(prm, grid, s);
+    }
+}
+
+}  // namespace exl3
+
+extern "C" int exl3_gemv_workspace(const exl3_gemv_desc* desc, size_t* partial_bytes, size_t* counter_bytes)
+{
+    using namespace exl3;
+    GemvLaunch L;
+    if (int e = plan_gemv(desc, &L)) return e;
+    if (partial_bytes) *partial_bytes = (size_t)L.grid * L.J * kRedStride * sizeof(float);
+    if (counter_bytes) *counter_bytes = (size_t)(L.blocks + 1) * sizeof(uint32_t);
+    return EXL3_OK;
+}
+
+extern "C" int exl3_gemv_reset(uint32_t* counters, size_t counter_bytes, void* stream)
+{
+    if (!counters) return EXL3_E_NULL;
+    return cudaMemsetAsync(counters, 0, counter_bytes, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? EXL3_OK
+               : EXL3_E_CUDA;
+}
+
+extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
+                         void* y, float* partials, uint32_t* counters, void* stream)
+{
+    using namespace exl3;
+    GemvLaunch L;
+    if (int e = plan_gemv(desc, &L)) return e;
+    if (!xh || !trellis || !svh || !y || !partials || !counters) return EXL3_E_NULL;
+    for (int m = 0; m < desc->n_members; ++m) {
+        if (!trellis[m]) return EXL3_E_NULL;
+        if (!aligned(trellis[m], 16)) return EXL3_E_ALIGN;
+    }
+    if (!aligned(xh, 4) || !aligned(svh, 2) || !aligned(y, 2) || !aligned(partials, 16) || !aligned(counters, 4))
+        return EXL3_E_ALIGN;
+    if (int e = check_device()) return e;
+
+    GemvParams prm{};
+    int off = 0;
+    for (int m = 0; m < 3; ++m) {
+        const int mm = m < desc->n_members ? m : 0;
+        prm.trellis[m] = trellis[mm];
+        prm.nt_member[m] = desc->n[mm] / 16;
+        prm.blk_off[m] = off;
+        if (m < desc->n_members) off += desc->n[m] / 128;
+    }
+    prm.blk_off[3] = off;
+    for (int m = desc->n_members; m < 3; ++m) prm.blk_off[m] = off + 1;   // never matched
+    prm.nm = desc->n_members;
+    prm.xh = static_cast<const __half*>(xh);
+    prm.svh = static_cast<const __half*>(svh);
+    prm.y = y;
+    prm.partials = partials;
+    prm.counters = counters;
+    prm.k = desc->k;
+    prm.KT = L.KT;
+    prm.rows = desc->rows;
+    prm.n_total = off * 128;
+    prm.blocks = L.blocks;
+    prm.out_bf16 = desc->out_dtype == EXL3_BF16;
+    prm.J = L.J;
+    prm.row_exact = (desc->flags & EXL3_GEMV_ROW_EXACT) != 0;
+    prm.units = L.units;
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (desc->bits) {
+    case 1: return launch_gemv_cb<1>(desc->codebook, prm, L.grid, s);
+    case 2: return launch_gemv_cb<2>(desc->codebook, prm, L.grid, s);
+    case 3: return launch_gemv_cb<3>(desc->codebook, prm, L.grid, s);
+    case 4: return launch_gemv_cb<4>(desc->codebook, prm, L.grid, s);
+    case 5: return launch_gemv_cb<5>(desc->codebook, prm, L.grid, s);
+    case 6: return launch_gemv_cb<6>(desc->codebook, prm, L.grid, s);
+    case 7: return launch_gemv_cb<7>(desc->codebook, prm, L.grid, s);
+    default: return launch_gemv_cb<8>(desc->codebook, prm, L.grid, s);
+    }
+}

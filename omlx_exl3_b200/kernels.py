@@ -1,0 +1,171 @@
+"""Host side of the EXL3 kernels: the reference's kernels.py interface over the sm_100a C ABI.
+
+Mirrors daig/omlx-exl3 src/omlx/exl3/kernels.py (same names, argument meaning and preconditions),
+with torch CUDA tensors in place of MLX arrays:
+
+  TrellisGemvPlan   kernels.py:263-299   decode GEMV (rows <= MAX_GEMV_ROWS), 1-3 sibling members
+  decode_wt         kernels.py:340-351   trellis -> W^T (n_chunk, k) fp16, bit-exact
+  rot               kernels.py:451-458   xh = had128(x * suh) / sqrt(128), member-major (NM, rows, k)
+  norm_rot          kernels.py:461-473   RMSNorm (MLX rounding) + rotations
+  swiglu_rot        kernels.py:476-483   had128(silu(g) * u * suh) / sqrt(128)
+
+Every op launches native code from libexl3b200.so on the current CUDA stream; nothing here falls back
+to another implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+from ._lib import GemvDesc, check, dtype_code, lib, ptr, stream_ptr
+
+MAX_GEMV_ROWS = 8
+# Default for new plans: True makes every GEMV row-exact (one row takes the tensor-core path too, so a
+# speculative-verify row gives the same bits as plain decoding); env OMLX_EXL3_ROW_EXACT=1.
+ROW_EXACT = os.environ.get("OMLX_EXL3_ROW_EXACT") == "1"
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("EXL3 kernels take CUDA tensors")
+
+
+class TrellisGemvPlan:
+    """y = had128(xh @ W_inner) * svh (out_dtype) for one EXL3 linear or a sibling group of <= 3
+    members sharing K and codebook. xh is (n_members, rows, k): each member's own rotated input.
+
+    The plan owns the launch descriptor, an fp16 copy of svh and the scratch (split-k partials and
+    per-block arrival counters that every call leaves at zero). One plan must not run on two streams
+    at once (the reference plan has the same restriction, kernels.py:284-286)."""
+
+    def __init__(self, k: int, member_ns: list[int], K: int, cb: int, svh: torch.Tensor, rows: int,
+                 out_dtype: torch.dtype = torch.float16, grid: int = 0, row_exact: bool | None = None):
+        assert k % 16 == 0 and all(n % 128 == 0 for n in member_ns) and 1 <= K <= 8 and cb in (0, 1, 2)
+        assert 1 <= len(member_ns) <= 3 and 1 <= rows <= MAX_GEMV_ROWS
+        assert out_dtype in (torch.float16, torch.bfloat16)
+        self.k, self.n, self.K, self.cb, self.rows = k, sum(member_ns), K, cb, rows
+        self.out_dtype = out_dtype
+        self.nsub = len(member_ns)
+        self.member_ns = list(member_ns)
+        self.KT, self.NT = k // 16, self.n // 16
+        self.blocks = self.n // 128
+        d = GemvDesc()
+        d.k, d.n_members = k, self.nsub
+        for i in range(3):
+            d.n[i] = member_ns[i] if i < self.nsub else 0
+        d.bits, d.codebook, d.rows = K, cb, rows
+        d.out_dtype = dtype_code(out_dtype)
+        d.grid = grid
+        self.row_exact = ROW_EXACT if row_exact is None else row_exact
+        d.flags = _lib.GEMV_ROW_EXACT if self.row_exact else 0
+        self.desc = d
+        self.device = svh.device
+        _need_cuda(svh)
+        pb, cbytes = ctypes.c_size_t(), ctypes.c_size_t()
+        with torch.cuda.device(self.device):
+            check(lib().exl3_gemv_workspace(ctypes.byref(d), ctypes.byref(pb), ctypes.byref(cbytes)),
+                  "exl3_gemv_workspace")
+            self.svh = svh.to(torch.float16).reshape(-1).contiguous()
+            assert self.svh.numel() == self.n
+            self.partials = torch.empty(max(pb.value // 4, 4), dtype=torch.float32, device=self.device)
+            self.counters = torch.zeros(max(cbytes.value // 4, 1), dtype=torch.int32, device=self.device)
+        self._tptr = (ctypes.c_void_p * 3)()
+
+    def workspace_status(self) -> int:
+        """The kernel's error word (0 = no bounded wait ever gave up)."""
+        return int(self.counters[self.blocks].item())
+
+    def __call__(self, xh: torch.Tensor, trellises: list[torch.Tensor], out: torch.Tensor | None = None) -> torch.Tensor:
+        """trellises: one flat uint32/int32 view per member. Returns (rows, n) in out_dtype."""
+        assert len(trellises) == self.nsub
+        xh = xh.contiguous()
+        if xh.dtype != torch.float16:
+            raise TypeError("xh must be fp16")
+        if xh.numel() != self.nsub * self.rows * self.k:
+            raise ValueError(f"xh has {xh.numel()} elements, expected {self.nsub}x{self.rows}x{self.k}")
+        _need_cuda(xh, *trellises)
+        for t, n in zip(trellises, self.member_ns):
+            if t.numel() * t.element_size() != self.k * n * self.K // 8:
+                raise ValueError(f"trellis holds {t.numel() * t.element_size()} bytes, expected "
+                                 f"{self.k * n * self.K // 8} for {self.k}x{n} at {self.K} bpw")
+        y = out if out is not None else torch.empty((self.rows, self.n), dtype=self.out_dtype, device=xh.device)
+        for i in range(3):
+            self._tptr[i] = trellises[i if i < self.nsub else 0].data_ptr()
+        check(lib().exl3_gemv(ctypes.byref(self.desc), xh.data_ptr(), ctypes.cast(self._tptr, ctypes.c_void_p),
+                              self.svh.data_ptr(), y.data_ptr(), self.partials.data_ptr(), self.counters.data_ptr(),
+                              stream_ptr(xh.device)), "exl3_gemv")
+        return y
+
+
+def decode_wt(trellis_u32: torch.Tensor, k: int, n: int, K: int, cb: int, nt0: int = 0, ntc: int | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """W_inner^T columns [16*nt0, 16*(nt0+ntc)) as an (16*ntc, k) fp16 matrix (rows = output features)."""
+    ntc = n // 16 - nt0 if ntc is None else ntc
+    _need_cuda(trellis_u32)
+    if trellis_u32.numel() * trellis_u32.element_size() < k * n * K // 8:
+        raise ValueError(f"trellis holds {trellis_u32.numel() * trellis_u32.element_size()} bytes, "
+                         f"expected {k * n * K // 8} for {k}x{n} at {K} bpw")
+    w = out if out is not None else torch.empty((ntc * 16, k), dtype=torch.float16, device=trellis_u32.device)
+    check(lib().exl3_decode_wt(trellis_u32.data_ptr(), k, n, K, cb, nt0, ntc, w.data_ptr(),
+                               stream_ptr(trellis_u32.device)), "exl3_decode_wt")
+    return w
+
+
+def rot(x: torch.Tensor, suh: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x (rows, K) any float dtype, suh (NM, K) fp16 -> xh (NM, rows, K) fp16."""
+    rows, k = x.shape
+    suh = suh.reshape(-1, k)
+    nm = suh.shape[0]
+    _need_cuda(x, suh)
+    x = x.contiguous()
+    suh = suh.to(torch.float16).contiguous()
+    xh = out if out is not None else torch.empty((nm, rows, k), dtype=torch.float16, device=x.device)
+    check(lib().exl3_rot(x.data_ptr(), dtype_code(x.dtype), rows, k, suh.data_ptr(), nm, xh.data_ptr(),
+                         stream_ptr(x.device)), "exl3_rot")
+    return xh
+
+
+def norm_rot(x: torch.Tensor, w: torch.Tensor, eps: float, suh: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm(x) * w in x.dtype (as mx.fast.rms_norm rounds it) and its rotations xh (NM, rows, K) fp16."""
+    rows, k = x.shape
+    suh = suh.reshape(-1, k)
+    nm = suh.shape[0]
+    assert k % 1024 == 0 and x.dtype in (torch.bfloat16, torch.float16)
+    _need_cuda(x, w, suh)
+    x = x.contiguous()
+    w = w.to(x.dtype).contiguous()
+    suh = suh.to(torch.float16).contiguous()
+    xn = torch.empty_like(x)
+    xh = torch.empty((nm, rows, k), dtype=torch.float16, device=x.device)
+    check(lib().exl3_norm_rot(x.data_ptr(), w.data_ptr(), dtype_code(x.dtype), rows, k, float(eps), suh.data_ptr(),
+                              nm, xn.data_ptr(), xh.data_ptr(), stream_ptr(x.device)), "exl3_norm_rot")
+    return xn, xh
+
+
+def swiglu_rot(gu: torch.Tensor, suh: torch.Tensor) -> torch.Tensor:
+    """gu (rows, 2N) = [gate | up], suh (N,) fp16 -> had128(silu(gate) * up * suh) / sqrt(128), (1, rows, N) fp16."""
+    rows, n2 = gu.shape
+    n = n2 // 2
+    _need_cuda(gu, suh)
+    gu = gu.contiguous()
+    suh = suh.to(torch.float16).reshape(-1).contiguous()
+    xh = torch.empty((1, rows, n), dtype=torch.float16, device=gu.device)
+    check(lib().exl3_swiglu_rot(gu.data_ptr(), dtype_code(gu.dtype), rows, n, suh.data_ptr(), xh.data_ptr(),
+                                stream_ptr(gu.device)), "exl3_swiglu_rot")
+    return xh
+
+
+def had_svh(y: torch.Tensor, svh: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+    """out_dtype(had128(y) / sqrt(128) * svh) for y (rows, n): the prefill output rotation (linear.py:105)."""
+    rows, n = y.shape
+    _need_cuda(y, svh)
+    y = y.contiguous()
+    svh = svh.to(torch.float16).reshape(-1).contiguous()
+    out = torch.empty((rows, n), dtype=out_dtype, device=y.device)
+    check(lib().exl3_had_svh(y.data_ptr(), dtype_code(y.dtype), rows, n, svh.data_ptr(), out.data_ptr(),
+                             dtype_code(out_dtype), stream_ptr(y.device)), "exl3_had_svh")
+    return out

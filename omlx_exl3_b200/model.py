@@ -1,0 +1,286 @@
+"""Qwen3-style dense decoder with EXL3 linears, tensor-parallel over the GPUs of one box.
+
+The reference runs its EXL3 linears inside mlx-vlm's Qwen3.5 model (not part of the reference repo);
+this module is the host model the EXL3 hot path is measured in (BASELINE configs 4 and 5): RMSNorm ->
+q/k/v (+ per-head q/k RMSNorm, RoPE) -> GQA attention over a KV cache -> o_proj -> residual ->
+RMSNorm -> SwiGLU MLP -> residual, then the final norm and an EXL3 output head. Module paths follow
+the Hugging Face checkpoint naming (model.layers.N.self_attn.q_proj, ..., lm_head), so a checkpoint's
+EXL3 tensors load by name (loader.py) and fusion.fuse_decode finds its targets.
+
+Tensor parallelism (tp_size > 1, one process per GPU): q/k/v, gate/up and the head are column-parallel
+(whole 128-column Hadamard blocks per rank), o_proj and down_proj row-parallel (whole 128-row blocks of
+k per rank, the input rotation is local per block); the row-parallel outputs are summed with one
+all-reduce each. The head's logits are gathered (or arg-maxed) across ranks.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+from torch import nn
+
+from .linear import EXL3Linear
+
+
+@dataclass
+class ModelConfig:
+    hidden_size: int = 5120
+    num_attention_heads: int = 40
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 17408
+    num_hidden_layers: int = 64
+    vocab_size: int = 151936
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1000000.0
+    max_position_embeddings: int = 8192
+    dtype: torch.dtype = torch.bfloat16
+    tie_word_embeddings: bool = False
+    extra: dict = field(default_factory=dict)
+
+    @staticmethod
+    def from_hf(cfg: dict) -> "ModelConfig":
+        c = cfg.get("text_config", cfg)
+        hd = c.get("head_dim") or c["hidden_size"] // c["num_attention_heads"]
+        dt = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}.get(
+            str(c.get("torch_dtype", "bfloat16")), torch.bfloat16)
+        return ModelConfig(hidden_size=c["hidden_size"], num_attention_heads=c["num_attention_heads"],
+                           num_key_value_heads=c.get("num_key_value_heads", c["num_attention_heads"]), head_dim=hd,
+                           intermediate_size=c["intermediate_size"], num_hidden_layers=c["num_hidden_layers"],
+                           vocab_size=c["vocab_size"], rms_norm_eps=c.get("rms_norm_eps", 1e-6),
+                           rope_theta=c.get("rope_theta", 1e6),
+                           max_position_embeddings=c.get("max_position_embeddings", 8192), dtype=dt,
+                           tie_word_embeddings=c.get("tie_word_embeddings", False))
+
+
+# ------------------------------------------------------------------------------------------ TP
+
+@dataclass
+class TP:
+    rank: int = 0
+    size: int = 1
+    group: object = None
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.size > 1:
+            dist.all_reduce(t, group=self.group)
+        return t
+
+    def blocks(self, n_blocks: int) -> tuple[int, int]:
+        """This rank's share [b0, b1) of n_blocks 128-wide blocks (uneven shares differ by one)."""
+        return n_blocks * self.rank // self.size, n_blocks * (self.rank + 1) // self.size
+
+
+def column_shard(n: int, tp: TP) -> tuple[int, int]:
+    """Output columns [c0, c1) of a column-parallel linear with n outputs on this rank."""
+    b0, b1 = tp.blocks(n // 128)
+    return b0 * 128, b1 * 128
+
+
+def row_shard(k: int, tp: TP) -> tuple[int, int]:
+    """Input rows [r0, r1) of a row-parallel linear with k inputs on this rank."""
+    b0, b1 = tp.blocks(k // 128)
+    return b0 * 128, b1 * 128
+
+
+# ------------------------------------------------------------------------------------------ layers
+
+class RMSNorm(nn.Module):
+    """RMSNorm with MLX's rounding (mx.fast.rms_norm): xn = T(w * T(x * rsqrt(mean(x^2) + eps)))."""
+
+    _exl3_rms_norm = True
+
+    def __init__(self, dim: int, eps: float, dtype: torch.dtype, device=None):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim, dtype=dtype, device=device), requires_grad=False)
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return (self.weight.float() * (xf * inv).to(x.dtype).float()).to(x.dtype)
+
+
+def rope_tables(cfg: ModelConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.head_dim, 2, dtype=torch.float64) / cfg.head_dim))
+    t = torch.arange(cfg.max_position_embeddings, dtype=torch.float64)
+    f = torch.outer(t, inv)
+    return torch.cos(f).float().to(device), torch.sin(f).float().to(device)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x (rows, heads, hd), cos/sin (rows, hd/2): rotate-half convention."""
+    xf = x.float()
+    h = xf.shape[-1] // 2
+    x1, x2 = xf[..., :h], xf[..., h:]
+    c, s = cos[:, None, :], sin[:, None, :]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1).to(x.dtype)
+
+
+class KVCache:
+    """Per-layer fp16 K/V cache (n_kv_local, max_len, head_dim) with a length counter."""
+
+    def __init__(self, n_layers: int, n_kv: int, max_len: int, head_dim: int, device, dtype=torch.float16):
+        self.k = [torch.zeros((n_kv, max_len, head_dim), dtype=dtype, device=device) for _ in range(n_layers)]
+        self.v = [torch.zeros((n_kv, max_len, head_dim), dtype=dtype, device=device) for _ in range(n_layers)]
+        self.max_len = max_len
+        self.length = 0
+
+    def fill_random(self, length: int, seed: int = 0):
+        g = torch.Generator(device=self.k[0].device)
+        g.manual_seed(seed)
+        for t in self.k + self.v:
+            t[:, :length].normal_(generator=g)
+        self.length = length
+
+
+def _exl3(k: int, n: int, K: int, device, cb: int = 0, bias: bool = False) -> EXL3Linear:
+    parts = {"trellis": ((k // 16, n // 16, 16 * K), torch.int16), "suh": ((k,), torch.float16),
+             "svh": ((n,), torch.float16)}
+    if cb == 1:
+        parts["mcg"] = ((1,), torch.int32)
+    elif cb == 2:
+        parts["mul1"] = ((1,), torch.int32)
+    if bias:
+        parts["bias"] = ((n,), torch.float16)
+    return EXL3Linear(k, n, parts, device=device)
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: ModelConfig, tp: TP, bits: dict, device):
+        super().__init__()
+        self.cfg, self.tp = cfg, tp
+        hd = cfg.head_dim
+        self.hq = cfg.num_attention_heads // tp.size
+        self.hkv = cfg.num_key_value_heads // tp.size
+        h = cfg.hidden_size
+        self.q_proj = _exl3(h, self.hq * hd, bits["q_proj"], device)
+        self.k_proj = _exl3(h, self.hkv * hd, bits["k_proj"], device)
+        self.v_proj = _exl3(h, self.hkv * hd, bits["v_proj"], device)
+        self.o_proj = _exl3(self.hq * hd, h, bits["o_proj"], device)
+        self.q_norm = RMSNorm(hd, cfg.rms_norm_eps, cfg.dtype, device)
+        self.k_norm = RMSNorm(hd, cfg.rms_norm_eps, cfg.dtype, device)
+
+    def forward(self, x: torch.Tensor, layer: int, cache: KVCache, pos: torch.Tensor, cos, sin) -> torch.Tensor:
+        rows = x.shape[0]
+        hd = self.cfg.head_dim
+        q = self.q_norm(self.q_proj(x).reshape(rows, self.hq, hd))
+        k = self.k_norm(self.k_proj(x).reshape(rows, self.hkv, hd))
+        v = self.v_proj(x).reshape(rows, self.hkv, hd)
+        c, s = cos.index_select(0, pos), sin.index_select(0, pos)
+        q, k = apply_rope(q, c, s), apply_rope(k, c, s)
+        kc, vc = cache.k[layer], cache.v[layer]
+        kc.index_copy_(1, pos, k.transpose(0, 1).to(kc.dtype))
+        vc.index_copy_(1, pos, v.transpose(0, 1).to(vc.dtype))
+        T = cache.length + rows
+        qh = q.transpose(0, 1)[None].to(kc.dtype)                  # (1, hq, rows, hd)
+        kk, vv = kc[None, :, :T], vc[None, :, :T]
+        mask = None
+        if rows > 1:   # causal among the new rows
+            i = torch.arange(rows, device=x.device)[:, None]
+            j = torch.arange(T, device=x.device)[None, :]
+            mask = (j <= (T - rows + i))[None, None]
+        o = F.scaled_dot_product_attention(qh, kk, vv, attn_mask=mask, enable_gqa=True)
+        o = o[0].transpose(0, 1).reshape(rows, self.hq * hd).to(x.dtype)
+        return self.tp.all_reduce(self.o_proj(o))
+
+
+class MLP(nn.Module):
+    def __init__(self, cfg: ModelConfig, tp: TP, bits: dict, device):
+        super().__init__()
+        ni = cfg.intermediate_size // tp.size
+        h = cfg.hidden_size
+        self.gate_proj = _exl3(h, ni, bits["gate_proj"], device)
+        self.up_proj = _exl3(h, ni, bits["up_proj"], device)
+        self.down_proj = _exl3(ni, h, bits["down_proj"], device)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: ModelConfig, tp: TP, bits: dict, device):
+        super().__init__()
+        self.tp = tp
+        self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, cfg.dtype, device)
+        self.self_attn = Attention(cfg, tp, bits, device)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, cfg.dtype, device)
+        self.mlp = MLP(cfg, tp, bits, device)
+
+    def forward(self, x, layer, cache, pos, cos, sin):
+        h = x + self.self_attn(self.input_layernorm(x), layer, cache, pos, cos, sin)
+        return h + self.tp.all_reduce(self.mlp(self.post_attention_layernorm(h)))
+
+
+class Inner(nn.Module):
+    def __init__(self, cfg: ModelConfig, tp: TP, layer_bits: list[dict], device):
+        super().__init__()
+        self.embed_tokens = nn.Embedding(cfg.vocab_size, cfg.hidden_size, device=device, dtype=cfg.dtype)
+        self.embed_tokens.weight.requires_grad_(False)
+        self.layers = nn.ModuleList([DecoderLayer(cfg, tp, b, device) for b in layer_bits])
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, cfg.dtype, device)
+
+
+class Qwen3EXL3(nn.Module):
+    """Decoder with EXL3 linears. forward(tokens, pos) -> this rank's logits (rows, vocab_local)."""
+
+    def __init__(self, cfg: ModelConfig, layer_bits: list[dict], head_bits: int | None, tp: TP | None = None,
+                 device=None):
+        super().__init__()
+        self.cfg = cfg
+        self.tp = tp or TP()
+        self.model = Inner(cfg, self.tp, layer_bits, device)
+        self.vocab_range = column_shard(((cfg.vocab_size + 127) // 128) * 128, self.tp)
+        v0, v1 = self.vocab_range
+        self.vocab_range = (v0, min(v1, cfg.vocab_size))
+        self.lm_head = _exl3(cfg.hidden_size, v1 - v0, head_bits, device) if head_bits else None
+        cos, sin = rope_tables(cfg, device)
+        self.register_buffer("rope_cos", cos, persistent=False)
+        self.register_buffer("rope_sin", sin, persistent=False)
+
+    def make_cache(self, max_len: int, device=None) -> KVCache:
+        dev = device or self.rope_cos.device
+        return KVCache(self.cfg.num_hidden_layers, self.cfg.num_key_value_heads // self.tp.size, max_len,
+                       self.cfg.head_dim, dev)
+
+    def hidden(self, tokens: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        x = self.model.embed_tokens(tokens)
+        for i, layer in enumerate(self.model.layers):
+            x = layer(x, i, cache, pos, self.rope_cos, self.rope_sin)
+        return self.model.norm(x)
+
+    def forward(self, tokens: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        h = self.hidden(tokens, cache, pos)
+        return self.lm_head(h) if self.lm_head is not None else h
+
+    def gather_logits(self, local: torch.Tensor) -> torch.Tensor:
+        """All ranks' logit shards -> (rows, vocab) on every rank."""
+        if self.tp.size == 1:
+            return local[:, : self.cfg.vocab_size]
+        n_local = torch.tensor([local.shape[1]], device=local.device)
+        sizes = [torch.zeros_like(n_local) for _ in range(self.tp.size)]
+        dist.all_gather(sizes, n_local, group=self.tp.group)
+        mx = int(max(s.item() for s in sizes))
+        pad = torch.zeros((local.shape[0], mx), dtype=local.dtype, device=local.device)
+        pad[:, : local.shape[1]] = local
+        parts = [torch.empty_like(pad) for _ in range(self.tp.size)]
+        dist.all_gather(parts, pad, group=self.tp.group)
+        out = torch.cat([p[:, : int(s.item())] for p, s in zip(parts, sizes)], dim=1)
+        return out[:, : self.cfg.vocab_size]
+
+    def greedy(self, local: torch.Tensor) -> torch.Tensor:
+        """Global argmax token per row from the local logit shard (one small all-gather)."""
+        v0 = self.vocab_range[0]
+        n_valid = self.vocab_range[1] - v0
+        val, idx = local[:, :n_valid].float().max(dim=-1)
+        if self.tp.size == 1:
+            return idx
+        pack = torch.stack([val, (idx + v0).float()], dim=-1)            # (rows, 2)
+        parts = [torch.empty_like(pack) for _ in range(self.tp.size)]
+        dist.all_gather(parts, pack, group=self.tp.group)
+        allp = torch.stack(parts)                                        # (tp, rows, 2)
+        best = allp[..., 0].argmax(dim=0)                                # (rows,)
+        return allp[best, torch.arange(pack.shape[0], device=pack.device), 1].long()

@@ -1,0 +1,26 @@
+"""Prefill (rows > MAX_GEMV_ROWS) path of EXL3Linear (daig/omlx-exl3 src/omlx/exl3/linear.py:97-121).
+
+xh = rot(x, suh) (fp16, as the reference casts the activations to fp16 before rotating), the
+trellis decoded to fp16 W^T in column chunks (kernels.decode_wt, bit-exact), the fp16 product,
+then the output rotation and svh (kernels.had_svh).
+"""
+from __future__ import annotations
+
+import torch
+
+from .kernels import decode_wt, had_svh, rot
+
+PREFILL_COL_CHUNK = 16384
+
+
+def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, cb: int, suh: torch.Tensor,
+                   svh: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """(rows, n) = had128(had128(x2 * suh) @ W) * svh for x2 (rows, k)."""
+    rows = x2.shape[0]
+    xh = rot(x2, suh.reshape(1, -1))[0]
+    y = torch.empty((rows, n), dtype=torch.float16, device=x2.device)
+    for c0 in range(0, n, PREFILL_COL_CHUNK):
+        c = min(PREFILL_COL_CHUNK, n - c0)
+        wt = decode_wt(tr, k, n, K, cb, nt0=c0 // 16, ntc=c // 16)
+        torch.matmul(xh, wt.t(), out=y[:, c0:c0 + c])
+    return had_svh(y, svh, out_dtype)
