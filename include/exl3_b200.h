@@ -89,6 +89,21 @@ typedef struct exl3_gemv_desc {
  * (the reference kernel's row-exact property, src/omlx/exl3/kernels.py:13-15). */
 enum { EXL3_GEMV_ROW_EXACT = 1 };
 
+/*
+ * Allocation-free variant of exl3_gemv. It has no counterpart in the reference: it exists for callers
+ * that cannot allocate device memory (code running during CUDA graph capture, hosts whose pool
+ * allocator owns all device memory, bindings that only receive input/output pointers). The split-k
+ * scratch lives in one fixed 4 MiB array inside this library (per device, held until exit), so a
+ * call whose scratch would not fit (more than 4095 column blocks of 128, or more than 4 MiB - 16 KiB
+ * of partials, e.g. a very wide output on a large grid) returns EXL3_E_WORKSPACE. The first call on
+ * each device looks the array's device address up; make that first call before any stream capture.
+ * Every call clears the counters it uses (one memset on `stream`). All calls on one device share the
+ * array, so calls that overlap on that GPU (e.g. on two streams) race and corrupt each other's
+ * results: issue them one after another on one stream. Each device has its own copy of the array.
+ */
+EXL3_API int exl3_gemv_noalloc(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
+                               const void* svh, void* y, void* stream);
+
 EXL3_API int exl3_gemv_workspace(const exl3_gemv_desc* desc, size_t* partial_bytes, size_t* counter_bytes);
 EXL3_API int exl3_gemv_reset(uint32_t* counters, size_t counter_bytes, void* stream);
 EXL3_API int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,

@@ -50,6 +50,7 @@ SIGNATURES = {
     "exl3_gemv_workspace": (_I, [ctypes.POINTER(GemvDesc), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
     "exl3_gemv_reset": (_I, [_P, _SZ, _P]),
     "exl3_gemv": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P, _P, _P]),
+    "exl3_gemv_noalloc": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P]),
     "exl3_rot": (_I, [_P, _I, _I, _I, _P, _I, _P, _P]),
     "exl3_norm_rot": (_I, [_P, _P, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
     "exl3_swiglu_rot": (_I, [_P, _I, _I, _I, _P, _P, _P]),

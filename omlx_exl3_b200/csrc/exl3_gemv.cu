@@ -25,6 +25,8 @@
 // * 1/sqrt(128) * svh, and writes y in the output dtype. No CTA ever waits on another CTA.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "exl3_b200.h"
 #include "exl3_common.cuh"
 #include "exl3_host.h"
@@ -465,4 +467,61 @@ extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint3
     case 7: return launch_gemv_cb<7>(desc->codebook, prm, L.grid, s);
     default: return launch_gemv_cb<8>(desc->codebook, prm, L.grid, s);
     }
+}
+
+// ---------------------------------------------------------------------------------------- no-alloc
+//
+// exl3_gemv_noalloc: the same GEMV for callers that cannot allocate device memory. Such callers
+// exist: code that runs while a CUDA graph is being captured (a cudaMalloc there breaks or
+// invalidates the capture), hosts that have handed all device memory to their own pool allocator and
+// forbid other allocations, and thin foreign-language bindings that only ever receive the input and
+// output pointers and have no way to own a scratch buffer. Instead of caller-provided scratch, this
+// entry point uses one fixed array in the library's device memory, sized below.
+
+namespace exl3 {
+
+// Scratch of the allocation-free entry point: arrival counters first, then split-k partials.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;                 // 4 MiB per device
+constexpr size_t kNoAllocCounterBytes = 16u << 10;                // up to 4095 blocks + status word
+static __device__ __align__(256) uint8_t g_gemv_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_gemv_noalloc_scratch for the current device, looked up once per device. In host
+// code the array's name is only a host-side stand-in, so the address must come from the runtime.
+static int noalloc_scratch(void** out)
+{
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return EXL3_E_CUDA;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch) != cudaSuccess || !p) return EXL3_E_CUDA;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return EXL3_OK;
+}
+
+}  // namespace exl3
+
+extern "C" int exl3_gemv_noalloc(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
+                                 const void* svh, void* y, void* stream)
+{
+    using namespace exl3;
+    GemvLaunch L;
+    if (int e = plan_gemv(desc, &L)) return e;
+    const size_t counter_bytes = (size_t)(L.blocks + 1) * sizeof(uint32_t);
+    const size_t partial_bytes = (size_t)L.grid * L.J * kRedStride * sizeof(float);
+    if (counter_bytes > kNoAllocCounterBytes || partial_bytes > kNoAllocScratchBytes - kNoAllocCounterBytes)
+        return EXL3_E_WORKSPACE;
+    if (int e = check_device()) return e;
+    void* base = nullptr;
+    if (int e = noalloc_scratch(&base)) return e;
+    uint32_t* counters = static_cast<uint32_t*>(base);
+    float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(base) + kNoAllocCounterBytes);
+    // The array keeps whatever the previous call left; the arrival counters must start at zero.
+    if (cudaMemsetAsync(counters, 0, counter_bytes, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return EXL3_E_CUDA;
+    return exl3_gemv(desc, xh, trellis, svh, y, partials, counters, stream);
 }
