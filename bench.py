@@ -314,6 +314,84 @@ def run_ours(args, rank, world, local_rank):
     return out
 
 
+# ------------------------------------------------------------------------------------------ decode
+
+def run_decode(args, rank, world, local_rank):
+    """batch-1 decode of the random-init 64-layer 27B-class model (hidden 5120,
+    40 q / 8 kv heads x 128, SwiGLU 17408, vocab 151936 with an 8-bpw EXL3 head, per-tensor bitrates
+    5..8 averaging 6.0) over a 4096-token random fp16 KV cache, tensor-parallel over the `world` GPUs
+    (NCCL all-reduce after o_proj and down_proj, logit arg-max gathered). One step = one token through
+    the captured decode graph; tok/s = steps / max over ranks of the device time."""
+    import torch
+    import torch.distributed as dist
+
+    from omlx_exl3_b200.decode import DecodeRunner
+    from omlx_exl3_b200.loader import draw_bits, synthetic_model
+    from omlx_exl3_b200.model import ModelConfig
+
+    dev = torch.device("cuda", local_rank)
+    cfg = ModelConfig(num_hidden_layers=args.decode_layers, max_position_embeddings=4200)
+    bits = draw_bits(cfg.num_hidden_layers, seed=0, cfg=cfg)
+    t_build = time.time()
+    model = synthetic_model(cfg, bits, 8, tp_rank=rank, tp_size=world, device=dev, seed=0)
+    cache = model.make_cache(4097)
+    cache.fill_random(4096, seed=1 + rank)
+    torch.cuda.synchronize(dev)
+    t_build = time.time() - t_build
+    runner = DecodeRunner(model, cache, rows=1, use_graph=True)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, args.warmup)):
+        runner.step()
+    torch.cuda.synchronize(dev)
+    n = max(20, args.steps)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        runner.step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = e0.elapsed_time(e1) / n
+
+    # end to end: the token goes in from (pinned) host memory and the next token comes back every step
+    tok_host = torch.tensor([17], dtype=torch.long).pin_memory()
+    out_host = torch.zeros(1, dtype=torch.long).pin_memory()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(n):
+        nxt = runner.step(tok_host.to(dev, non_blocking=True))
+        out_host.copy_(nxt, non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms_e2e = e2.elapsed_time(e3) / n
+
+    vals = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    runner.release()
+    weights = sum(b.numel() * b.element_size() for m in model.modules() for nm, b in m.named_buffers(recurse=False)
+                  if nm == "trellis")
+    del runner, model, cache
+    torch.cuda.empty_cache()
+    ms, ms_e2e = float(vals[0]), float(vals[1])
+    return {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 4), "tp": world, "steps": n,
+            "e2e_tok_s": round(1000.0 / ms_e2e, 2),
+            "trellis_bytes_per_gpu": int(weights),
+            "weight_stream_GBps_per_gpu": round(weights / (ms * 1e-3) / 1e9, 1),
+            "build_s": round(t_build, 1),
+            "model": f"random-init Qwen3-style, {cfg.num_hidden_layers} layers, hidden 5120, 40q/8kv x 128, "
+                     "SwiGLU 17408, vocab 151936 (8-bpw EXL3 head), per-group bpw 5..8 averaging 6.0, "
+                     "4096-token random fp16 KV cache, CUDA-graph decode step"}
+
+
 # ------------------------------------------------------------------------------------------ CPU
 
 def cpu_reference_sample(budget_s: float = 12.0):
@@ -397,6 +475,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, help="k,n,K,rows: one GEMV configuration instead of the sweep")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 27B-class TP decode measurement")
+    ap.add_argument("--decode-layers", type=int, default=64)
     args = ap.parse_args()
     select_case(args.case)
     args.warmup = max(args.warmup, 3)
@@ -419,7 +499,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:
         out = run_ours(args, rank, world, local_rank)
+        dec = None if (args.no_decode or args.case) else run_decode(args, rank, world, local_rank)
         if out is not None:
+            if dec is not None:
+                out["decode"] = dec
             if world == 1 and not args.no_cpu_baseline:
                 out["cpu_baseline"] = cpu_reference_sample(budget_s=12.0)
             print(json.dumps(out), flush=True)

@@ -271,42 +271,51 @@ def load(model_name: str | Path, *, tp_rank: int = 0, tp_size: int = 1, tp_group
 
 # ------------------------------------------------------------------------------ synthetic weights
 
+# Sibling tensors that self-calibrated EXL3 checkpoints quantize at one rate (k/v, gate/up), so that
+# they can share one GEMV launch; q, o and down get their own rates.
+_RATE_GROUPS = (("q_proj",), ("k_proj", "v_proj"), ("o_proj",), ("gate_proj", "up_proj"), ("down_proj",))
+
+
 def draw_bits(n_layers: int, seed: int, choices=(5, 6, 7, 8), target: float = 6.0, cfg: ModelConfig | None = None
               ) -> list[dict]:
     """Seeded per-tensor bitrates in 5..8 bpw whose weight-count-weighted mean is `target` (BASELINE
-    config 5). Draws, then nudges the largest-deviation tensors until the weighted mean is within 0.01."""
+    config 5). One rate per rate group (_RATE_GROUPS); drawn, then nudged group by group until the
+    weighted mean is within 0.01 of the target."""
     cfg = cfg or ModelConfig()
     h, hd, ni = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
     sizes = {"q_proj": h * cfg.num_attention_heads * hd, "k_proj": h * cfg.num_key_value_heads * hd,
              "v_proj": h * cfg.num_key_value_heads * hd, "o_proj": cfg.num_attention_heads * hd * h,
              "gate_proj": h * ni, "up_proj": h * ni, "down_proj": ni * h}
+    gsize = {grp: sum(sizes[nm] for nm in grp) for grp in _RATE_GROUPS}
     rng = np.random.default_rng(seed)
     p = np.array([0.35, 0.35, 0.2, 0.1])[: len(choices)]
     p = p / p.sum()
-    layers = [{name: int(rng.choice(choices, p=p)) for name in sizes} for _ in range(n_layers)]
-    total = sum(sizes.values()) * n_layers
+    groups = [{grp: int(rng.choice(choices, p=p)) for grp in _RATE_GROUPS} for _ in range(n_layers)]
+    total = sum(gsize.values()) * n_layers
 
     def mean():
-        return sum(sizes[nm] * b[nm] for b in layers for nm in sizes) / total
+        return sum(gsize[grp] * b[grp] for b in groups for grp in gsize) / total
 
-    order = [(li, nm) for li in range(n_layers) for nm in sizes]
+    order = [(li, grp) for li in range(n_layers) for grp in _RATE_GROUPS]
     rng.shuffle(order)
     it = 0
     while abs(mean() - target) > 0.01 and it < 100 * len(order):
-        li, nm = order[it % len(order)]
-        b = layers[li][nm]
+        li, grp = order[it % len(order)]
+        b = groups[li][grp]
+        # a step of the smallest groups first keeps the final mean close to the target
         if mean() > target and b > min(choices):
-            layers[li][nm] = b - 1
+            groups[li][grp] = b - 1
         elif mean() < target and b < max(choices):
-            layers[li][nm] = b + 1
+            groups[li][grp] = b + 1
         it += 1
-    return layers
+    return [{nm: b[grp] for grp in _RATE_GROUPS for nm in grp} for b in groups]
 
 
 def synthetic_model(cfg: ModelConfig, layer_bits: list[dict], head_bits: int | None, *, tp_rank: int = 0,
                     tp_size: int = 1, tp_group=None, device=None, seed: int = 0, fuse: bool = True,
-                    codebook: int = 0) -> Qwen3EXL3:
-    """Random-init model with seeded uniform trellis, +-1 suh/svh and N(1, 0.1) norm weights, generated
+                    codebook: int = 0, svh_scale: float = 1.0) -> Qwen3EXL3:
+    """Random-init model with seeded uniform trellis, +-1 suh, +-svh_scale/(1.244 sqrt(k)) svh (0 gives
+    +-1) and N(1, 0.1) norm weights, generated
     directly on the device. Every rank draws the same full tensors and keeps its shard, so any TP size
     describes the same model."""
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -326,7 +335,11 @@ def synthetic_model(cfg: ModelConfig, layer_bits: list[dict], head_bits: int | N
                                   device=device, generator=gen)
             tr = words.view(torch.int16)
             suh = torch.randint(0, 2, (k_full,), device=device, generator=gen).to(torch.float16) * 2 - 1
-            svh = torch.randint(0, 2, (n_full,), device=device, generator=gen).to(torch.float16) * 2 - 1
+            # +-svh_scale / sqrt(k): with decoded weights of std ~1.24 each linear keeps the activation
+            # scale, so a deep random model stays inside the fp16 range of the rotated inputs
+            sv = svh_scale / (1.244 * float(k_full) ** 0.5) if svh_scale else 1.0
+            svh = (torch.randint(0, 2, (n_full,), device=device, generator=gen).to(torch.float32) * 2 - 1) * sv
+            svh = svh.to(torch.float16)
             mod.trellis.copy_(shard_exl3_part("trellis", tr, kind, k_full, n_full, tp))
             mod.suh.copy_(shard_exl3_part("suh", suh, kind, k_full, n_full, tp))
             mod.svh.copy_(shard_exl3_part("svh", svh, kind, k_full, n_full, tp))

@@ -1,0 +1,127 @@
+"""GPU: the EXL3 decoder path (EXL3Linear / sibling groups / fused norms and MLP / decode graph) against
+the fp32 oracle forward, by logit KL (north star: KL <= 1e-4), plus the unfused and prefill paths."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model_oracle, oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _small_model(dev, fuse=True, bits=None, head_bits=8, layers=2, seed=3):
+    from omlx_exl3_b200.loader import synthetic_model
+    from omlx_exl3_b200.model import ModelConfig
+    cfg = ModelConfig(hidden_size=1024, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                      intermediate_size=2048, num_hidden_layers=layers, vocab_size=2048,
+                      max_position_embeddings=1024)
+    b = bits or {"q_proj": 6, "k_proj": 6, "v_proj": 6, "o_proj": 5, "gate_proj": 6, "up_proj": 6, "down_proj": 4}
+    return synthetic_model(cfg, [dict(b) for _ in range(layers)], head_bits, device=dev, seed=seed, fuse=fuse)
+
+
+def _kl(ref_logits, logits):
+    return O.kl_div(ref_logits, logits)
+
+
+@pytest.mark.parametrize("fuse", [True, False])
+@pytest.mark.parametrize("rows", [1, 3])
+def test_decode_logits_kl(cuda, fuse, rows):
+    torch.manual_seed(0)
+    model = _small_model(cuda, fuse=fuse)
+    cache = model.make_cache(512)
+    cache.fill_random(200, seed=1)
+    toks = torch.tensor([5, 77, 1999][:rows], device=cuda)
+    pos = torch.arange(200, 200 + rows, device=cuda)
+    ck = [c.float().cpu().numpy() for c in cache.k]
+    cv = [c.float().cpu().numpy() for c in cache.v]
+    with torch.no_grad():
+        logits = model(toks, cache, pos).float().cpu().numpy()
+    ref = model_oracle.forward(model, toks.cpu().numpy(), ck, cv, 200)
+    kl = _kl(ref, logits[:, : ref.shape[1]])
+    assert kl.mean() < 1e-4, kl
+    assert (logits.argmax(-1) == ref.argmax(-1)).all()
+
+
+def test_prefill_rows_match_oracle(cuda):
+    """rows > 8 goes through the prefill path (decode_wt + fp16 GEMM + output rotation)."""
+    model = _small_model(cuda, fuse=True, layers=1)
+    cache = model.make_cache(512)
+    cache.fill_random(64, seed=2)
+    rows = 16
+    toks = torch.arange(rows, device=cuda) * 37 % 2048
+    pos = torch.arange(64, 64 + rows, device=cuda)
+    ck = [c.float().cpu().numpy() for c in cache.k]
+    cv = [c.float().cpu().numpy() for c in cache.v]
+    with torch.no_grad():
+        logits = model(toks, cache, pos).float().cpu().numpy()
+    ref = model_oracle.forward(model, toks.cpu().numpy(), ck, cv, 64)
+    assert _kl(ref, logits).mean() < 1e-4
+
+
+def test_decode_runner_graph_matches_eager(cuda):
+    from omlx_exl3_b200.decode import DecodeRunner
+    model = _small_model(cuda, fuse=True)
+    cache = model.make_cache(512)
+    cache.fill_random(300, seed=4)
+    r_graph = DecodeRunner(model, cache, rows=1, use_graph=True)
+    a = r_graph.step(torch.tensor([11], device=cuda)).clone()
+    la = r_graph.logits.clone()
+    b = r_graph.step(torch.tensor([11], device=cuda)).clone()
+    assert torch.equal(a, b)
+    with torch.no_grad():
+        eager = model(torch.tensor([11], device=cuda), cache, torch.tensor([300], device=cuda))
+    assert torch.equal(la, eager)
+    assert int(a.item()) == int(eager.float().argmax(-1).item())
+
+
+def test_sibling_group_and_fusion_installed(cuda):
+    model = _small_model(cuda, fuse=True)
+    layer = model.model.layers[0]
+    g = layer.self_attn.q_proj._group
+    assert g is not None and g is layer.self_attn.k_proj._group and len(g.members) == 3
+    assert layer.mlp.gate_proj._group is layer.mlp.up_proj._group
+    assert type(layer.input_layernorm).__name__ == "RMSNorm" and "_exl3_target" in layer.input_layernorm.__dict__
+    # mixed bitrates: q alone, k/v grouped
+    m2 = _small_model(cuda, bits={"q_proj": 5, "k_proj": 6, "v_proj": 6, "o_proj": 5, "gate_proj": 6,
+                                  "up_proj": 6, "down_proj": 6})
+    at = m2.model.layers[0].self_attn
+    assert at.q_proj._group is None and at.k_proj._group is at.v_proj._group is not None
+
+
+def test_exl3linear_matches_oracle_rows(cuda):
+    from omlx_exl3_b200 import EXL3Linear
+    rng = np.random.default_rng(8)
+    k, n, K = 1024, 768, 5
+    t = O.random_trellis(k, n, K, 12)
+    suh = np.where(rng.random(k) < 0.5, -1, 1).astype(np.float16)
+    svh = (rng.standard_normal(n) * 0.02).astype(np.float16)
+    bias = rng.standard_normal(n).astype(np.float16)
+    lin = EXL3Linear(k, n, {"trellis": (t.shape, torch.int16), "suh": ((k,), torch.float16),
+                            "svh": ((n,), torch.float16), "bias": ((n,), torch.float16)}, device=cuda)
+    lin.load_state_dict({"trellis": torch.from_numpy(t), "suh": torch.from_numpy(suh), "svh": torch.from_numpy(svh),
+                         "bias": torch.from_numpy(bias)})
+    for rows in (1, 2, 8, 9, 33):
+        x = rng.standard_normal((rows, k)).astype(np.float32)
+        for dt in (torch.float16, torch.bfloat16):
+            y = lin(torch.from_numpy(x).to(cuda, dt)).float().cpu().numpy()
+            ref = O.linear_forward(t, k, n, K, 0, torch.from_numpy(x).to(dt).float().numpy(), suh, svh, bias)
+            assert O.max_rel(y, ref) < 1e-2, (rows, dt)
+
+
+def test_legacy_packed_signs(cuda):
+    from omlx_exl3_b200 import EXL3Linear
+    rng = np.random.default_rng(9)
+    k, n, K = 512, 256, 4
+    t = O.random_trellis(k, n, K, 13)
+    su = rng.integers(0, 2 ** 16, k // 16, dtype=np.uint32).astype(np.uint16).view(np.int16)
+    sv = rng.integers(0, 2 ** 16, n // 16, dtype=np.uint32).astype(np.uint16).view(np.int16)
+    lin = EXL3Linear(k, n, {"trellis": (t.shape, torch.int16), "su": ((k // 16,), torch.int16),
+                            "sv": ((n // 16,), torch.int16), "mcg": ((1,), torch.int32)}, device=cuda)
+    lin.load_state_dict({"trellis": torch.from_numpy(t), "su": torch.from_numpy(su), "sv": torch.from_numpy(sv),
+                         "mcg": torch.zeros(1, dtype=torch.int32)})
+    x = rng.standard_normal((2, k)).astype(np.float32)
+    y = lin(torch.from_numpy(x).to(cuda, torch.float16)).float().cpu().numpy()
+    ref = O.linear_forward(t, k, n, K, 1, x.astype(np.float16).astype(np.float32), O.unpack_signs(su),
+                           O.unpack_signs(sv))
+    assert lin._cb == 1
+    assert O.max_rel(y, ref) < 1e-2
