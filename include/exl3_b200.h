@@ -133,6 +133,17 @@ EXL3_API int exl3_norm_rot(const void* x, const void* w, int dtype, int rows, in
 EXL3_API int exl3_swiglu_rot(const void* gu, int gu_dtype, int rows, int n, const void* suh, void* xh, void* stream);
 
 /*
+ * Prefill GEMM with the trellis decoded in-kernel (tcgen05 / tensor memory):
+ *   y = out_dtype( had128(xh @ W) / sqrt(128) * svh ),  xh fp16 (M, k), W the k x n trellis, y (M, n).
+ * Replaces: EXL3Linear._prefill (src/omlx/exl3/linear.py:97-105: decode_wt chunks, MLX matmul, _had128,
+ * * svh). k % 64 == 0, n % 128 == 0, any M >= 1; out_dtype EXL3_F16, EXL3_BF16 or EXL3_F32. `status`
+ * is a device uint32 that the kernel ORs an error bit into if a bounded wait gives up (0 = fine).
+ * xh, trellis and y must be 16-byte aligned.
+ */
+EXL3_API int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* trellis, int bits, int codebook,
+                       const void* svh, void* y, int out_dtype, uint32_t* status, void* stream);
+
+/*
  * Output rotation: out[r, :] = out_dtype(had128(y[r, :]) / sqrt(128) * svh), y (rows, n) of y_dtype.
  * Replaces: the prefill tail `_had128(y) * self._svh` (src/omlx/exl3/linear.py:105, :31-33).
  * svh: fp16 (n); n % 128 == 0.

@@ -214,7 +214,7 @@ __device__ __forceinline__ void hashes8(const uint32_t (&w)[3], uint32_t (&h)[8]
 #define EXL3_JUNK(J)                                                                            \
     if constexpr (JM & (1u << J)) {                                                             \
         constexpr int SH = (7 - J) * K;                                                         \
-        constexpr bool kFromState = 16 % K == 0 && J >= 16 / K && !(JM & (1u << (J - 16 / K))); \
+        constexpr bool kFromState = 16 % K == 0 && J >= 16 / K && !(JM & (1u << ((J - 16 / K) & 7))); \
         const uint32_t X = state_loose<SH, kFromState>(w);                                      \
         uint32_t Jv;                                                                            \
         if constexpr (kFromState) Jv = s[(J - 16 / K) & 7];                                     \

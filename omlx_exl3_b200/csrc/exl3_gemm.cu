@@ -1,0 +1,445 @@
+// EXL3 prefill GEMM for sm_100a: y = had128(xh @ W) / sqrt(128) * svh, W decoded from the trellis
+// inside the kernel and fed to the 5th-generation tensor cores.
+//
+// Replaces the reference's prefill path (daig/omlx-exl3 src/omlx/exl3/linear.py:97-121: decode_wt
+// of 16384-column chunks to fp16 in memory, MLX matmul, _had128, * svh). Here nothing but xh, the
+// trellis and y touch HBM.
+//
+// CTA tile: 256 rows of xh (two M=128 halves) x 128 output columns (one Hadamard block) x the whole k,
+// in k-steps of 64. Per k-step and pipeline stage:
+//   - warp 0 (one lane) loads the 256 x 64 fp16 xh tile with one TMA tensor load (128B swizzle);
+//   - warps 2..9 decode the 4 x 8 trellis tiles of the step (16 k-rows x 16 columns each; one lane =
+//     8 consecutive stream positions, exl3_common.cuh) to exact fp16 weights and store them straight
+//     into the 128 x 64 B tile in the same K-major 128B-swizzled layout the tensor core reads;
+//   - warp 1 (one lane) issues 2 x 4 tcgen05.mma (M=128, N=128, K=16, fp16 in, fp32 accumulate in
+//     tensor memory) and commits them to the stage's "empty" barrier.
+// The epilogue warps (2..9) read one accumulator row per thread (tcgen05.ld 32x32b: 128 fp32 columns),
+// run the 128-point FWHT in registers (stage order 1..64, as the reference), scale by 1/sqrt(128) and
+// svh, and store y. Every wait is bounded (exl3_common.cuh mbar_wait): a lost completion sets a status
+// bit instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "exl3_b200.h"
+#include "exl3_common.cuh"
+#include "exl3_host.h"
+
+namespace exl3 {
+
+constexpr int kGemmBM = 256;                  // rows of xh per CTA (two M=128 MMAs)
+constexpr int kGemmBN = 128;                  // output columns per CTA
+constexpr int kGemmBK = 64;                   // k per pipeline stage (128 bytes of fp16: one swizzle row)
+constexpr int kGemmStages = 3;
+constexpr int kGemmDecWarps = 8;
+constexpr int kGemmThreads = 32 * (2 + kGemmDecWarps);
+constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;   // 32 KB
+constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;   // 16 KB
+constexpr int kGemmDecDepth = 4;              // trellis k-steps in flight per decoder warp
+// + per decoder warp a ring of kGemmDecDepth x 4 tiles x 32K bytes (K <= 8: 256 bytes per tile)
+constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmABytes + kGemmBBytes) + 256 + kGemmDecWarps * kGemmDecDepth * 4 * 256;
+
+struct GemmParams {
+    const uint32_t* trellis;
+    const __half* svh;
+    void* y;
+    uint32_t* status;
+    int M, k, n, KT, NT, out_dtype;
+};
+
+// ------------------------------------------------------------------------------ tcgen05 / TMA PTX
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p)
+{
+    const uint64_t addr = smem_addr(p);
+    uint64_t d = (addr >> 4) & 0x3FFFull;          // start address
+    d |= (uint64_t)(16 >> 4) << 16;                // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset: next 8-row group
+    d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                        // layout: 128B swizzle
+    return d;
+}
+
+// Instruction descriptor: fp16 A/B, fp32 D, both K-major, M x N.
+constexpr uint32_t idesc_f16_f32(int M, int N)
+{
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------------------------------------ decode into B
+// Byte offset of (row n, k) inside a K-major 128B-swizzled tile whose rows are 128 bytes (64 fp16):
+// 16-byte chunk index XOR (row mod 8), 8-row groups of 1024 bytes.
+__device__ __forceinline__ uint32_t sw128_offset(int n, int kbyte)
+{
+    return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((kbyte >> 4) ^ (n & 7))) << 4) + (kbyte & 15));
+}
+
+template <int CB>
+__device__ __forceinline__ uint32_t pack_weights(uint32_t sa, uint32_t sb)
+{
+    if constexpr (CB == 2) {
+        return __byte_perm(sa, sb, 0x5410);        // (w_a, w_b): the mul1 split word is (w, 0)
+    } else {
+        const uint32_t lo = __byte_perm(sa, sb, 0x5410), hi = __byte_perm(sa, sb, 0x7632);
+        const __half2 w = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+        return *reinterpret_cast<const uint32_t*>(&w);
+    }
+}
+
+template <typename OT>
+__device__ __forceinline__ void store_row128(OT* dst, const float (&v)[128], const __half* svh)
+{
+#pragma unroll
+    for (int c = 0; c < 128; c += 8) {
+        if constexpr (sizeof(OT) == 4) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[c + i] = from_f32<OT>(v[c + i] * kHadScale * __half2float(svh[c + i]));
+        } else {
+            uint32_t pk[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const OT a = from_f32<OT>(v[c + 2 * i] * kHadScale * __half2float(svh[c + 2 * i]));
+                const OT b = from_f32<OT>(v[c + 2 * i + 1] * kHadScale * __half2float(svh[c + 2 * i + 1]));
+                pk[i] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&a)) |
+                        ((uint32_t)(*reinterpret_cast<const uint16_t*>(&b)) << 16);
+            }
+            *reinterpret_cast<uint4*>(dst + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+    }
+}
+
+template <int K, int CB>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* As = smem;                                         // stages x 32 KB
+    uint8_t* Bs = smem + kGemmStages * kGemmABytes;             // stages x 16 KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(Bs + kGemmStages * kGemmBBytes);
+    uint64_t* full = bars;                                      // xh tile landed
+    uint64_t* decoded = bars + kGemmStages;                     // B tile written by the decoders
+    uint64_t* empty = bars + 2 * kGemmStages;                   // MMAs of the stage done
+    uint64_t* accum = bars + 3 * kGemmStages;                   // all MMAs done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kGemmStages + 1);
+
+    constexpr int TW = 8 * K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = blockIdx.x;                                  // 128-column block
+    const int m0 = blockIdx.y * kGemmBM;
+    const int nsteps = p.k / kGemmBK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&decoded[s], kGemmDecWarps);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        // 256 TMEM columns: two 128 x 128 fp32 accumulators
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- xh producer (TMA)
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+            for (int i = 0; i < nsteps; ++i) {
+                const int s = i % kGemmStages;
+                if (i >= kGemmStages && !mbar_wait(&empty[s], ((i / kGemmStages) - 1) & 1)) {
+                    atomicOr(p.status, kStatusPipeTimeout);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], kGemmABytes);
+                tma_load_2d(As + s * kGemmABytes, &xmap, i * kGemmBK, m0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(128, kGemmBN);
+            bool ok = true;
+            for (int i = 0; i < nsteps && ok; ++i) {
+                const int s = i % kGemmStages;
+                const uint32_t par = (i / kGemmStages) & 1;
+                if (!mbar_wait(&full[s], par) || !mbar_wait(&decoded[s], par)) {
+                    atomicOr(p.status, kStatusPipeTimeout);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint64_t bdesc = smem_desc_sw128(Bs + s * kGemmBBytes + kk * 32);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint64_t adesc = smem_desc_sw128(As + s * kGemmABytes + h * (kGemmABytes / 2) + kk * 32);
+                        tc_mma_f16(tmem + h * kGemmBN, adesc, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
+                tc_commit(&empty[s]);
+            }
+            tc_commit(accum);
+        }
+    } else {
+        // ---------------------------------------------------------------- decoders, then epilogue
+        const int dw = warp - 2;                                // 0..7
+        const int g = lane >> 2, q = lane & 3;
+        const LaneWindow<K> lw(lane);
+        // warp dw decodes k-slice dw / 2 and the four n-tiles 4 * (dw % 2) .. +3 of every k-step
+        constexpr int kTiles = 4;
+        const int ktl = dw >> 1, nt_base = (dw & 1) * kTiles;
+        // The warp's tiles of a k-step are contiguous (kTiles * TW words); they are streamed into a
+        // private ring of kGemmDecDepth slots with cp.async, kGemmDecDepth - 1 steps ahead.
+        uint32_t* dring = reinterpret_cast<uint32_t*>(Bs + kGemmStages * kGemmBBytes + 256) +
+                          (size_t)dw * kGemmDecDepth * kTiles * TW;
+        int fstep = 0, fslot = 0, cslot = 0;
+        auto fetch = [&]() {
+            if (fstep < nsteps) {
+                const uint32_t* src = p.trellis +
+                                      ((size_t)(fstep * (kGemmBK / 16) + ktl) * p.NT + (size_t)nb * 8 + nt_base) * TW;
+                uint32_t* dst = dring + (size_t)fslot * kTiles * TW;
+                for (int c = lane; c < kTiles * TW / 4; c += 32) cp_async16(dst + c * 4, src + c * 4);
+            }
+            ++fstep;
+            cp_async_commit();
+            fslot = fslot + 1 == kGemmDecDepth ? 0 : fslot + 1;
+        };
+#pragma unroll 1
+        for (int d = 0; d < kGemmDecDepth - 1; ++d) fetch();
+        bool ok = true;
+        for (int i = 0; i < nsteps && ok; ++i) {
+            const int s = i % kGemmStages;
+            fetch();
+            if (i >= kGemmStages && !mbar_wait(&empty[s], ((i / kGemmStages) - 1) & 1)) {
+                atomicOr(p.status, kStatusPipeTimeout);
+                ok = false;
+            }
+            cp_async_wait<kGemmDecDepth - 1>();
+            __syncwarp();
+            const uint32_t* stage_tiles = dring + (size_t)cslot * kTiles * TW;
+            cslot = cslot + 1 == kGemmDecDepth ? 0 : cslot + 1;
+            uint8_t* B = Bs + s * kGemmBBytes;
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t) {
+                const int ntl = nt_base + t;
+                const uint32_t* tile = stage_tiles + t * TW;
+                uint32_t w[3], hsh[8], a[8];
+                window_words<K>(tile, lw, w);
+                hashes8<K, CB>(w, hsh);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[j] = split_from_hash<CB>(hsh[j]);
+                // lane holds column g (positions 0..3) and g+8 (4..7) at k 2q, 2q+1, 2q+8, 2q+9
+                const int n_lo = ntl * 16 + g, n_hi = n_lo + 8;
+                const int kb = ktl * 32 + 4 * q;                // byte of k = 16*ktl + 2q in the 128-byte row
+                const uint32_t o0 = sw128_offset(n_lo, kb), o1 = sw128_offset(n_lo, kb + 16);
+                const uint32_t o2 = sw128_offset(n_hi, kb), o3 = sw128_offset(n_hi, kb + 16);
+                const uint32_t w0 = pack_weights<CB>(a[0], a[1]), w1 = pack_weights<CB>(a[2], a[3]);
+                const uint32_t w2 = pack_weights<CB>(a[4], a[5]), w3 = pack_weights<CB>(a[6], a[7]);
+                *reinterpret_cast<uint32_t*>(B + o0) = w0;
+                *reinterpret_cast<uint32_t*>(B + o1) = w1;
+                *reinterpret_cast<uint32_t*>(B + o2) = w2;
+                *reinterpret_cast<uint32_t*>(B + o3) = w3;
+            }
+            fence_proxy_async_smem();                           // generic-proxy writes -> tensor core reads
+            __syncwarp();                                       // also: the ring slot may be refilled
+            if (lane == 0) mbar_arrive(&decoded[s]);
+        }
+        cp_async_wait<0>();                                     // no copy in flight past this point
+
+        // ---- epilogue: one accumulator row per thread
+        const int h = dw >> 2;                                  // M half
+        const int quarter = warp & 3;                           // TMEM lanes this warp may access
+        const int row = m0 + h * 128 + quarter * 32 + lane;
+        const bool done = mbar_wait(accum, 0);
+        if (!done) atomicOr(p.status, kStatusPipeTimeout);
+        tc_fence_after();
+        float v[128];
+        const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float part[32];
+            tc_ld32(tbase + c * 32, part);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[c * 32 + i] = part[i];
+        }
+        if (done && row < p.M) {
+#pragma unroll
+            for (int hs = 1; hs < 128; hs <<= 1) {
+#pragma unroll
+                for (int b = 0; b < 64; ++b) {
+                    const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
+                    const float a0 = v[i0], a1 = v[i1];
+                    v[i0] = a0 + a1;
+                    v[i1] = a0 - a1;
+                }
+            }
+            const __half* sv = p.svh + (size_t)nb * kGemmBN;
+            const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN;
+            if (p.out_dtype == EXL3_F16) store_row128(static_cast<__half*>(p.y) + off, v, sv);
+            else if (p.out_dtype == EXL3_BF16) store_row128(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
+            else store_row128(static_cast<float*>(p.y) + off, v, sv);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+    }
+}
+
+// ------------------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+template <int K, int CB>
+static int launch_gemm_k(const CUtensorMap& map, const GemmParams& prm, dim3 grid, cudaStream_t s)
+{
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(gemm_kernel<K, CB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
+            cudaSuccess)
+            return EXL3_E_CUDA;
+        attr_set[dev] = true;
+    }
+    gemm_kernel<K, CB><<<grid, kGemmThreads, kGemmSmem, s>>>(map, prm);
+    return launch_status();
+}
+
+template <int K>
+static int launch_gemm_cb(int cb, const CUtensorMap& map, const GemmParams& prm, dim3 grid, cudaStream_t s)
+{
+    switch (cb) {
+    case 0: return launch_gemm_k<K, 0>(map, prm, grid, s);
+    case 1: return launch_gemm_k<K, 1>(map, prm, grid, s);
+    default: return launch_gemm_k<K, 2>(map, prm, grid, s);
+    }
+}
+
+}  // namespace exl3
+
+extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* trellis, int bits, int codebook,
+                         const void* svh, void* y, int out_dtype, uint32_t* status, void* stream)
+{
+    using namespace exl3;
+    if (!xh || !trellis || !svh || !y || !status) return EXL3_E_NULL;
+    if (M < 1 || k <= 0 || n <= 0 || k % kGemmBK || n % kGemmBN) return EXL3_E_SHAPE;
+    if (bits < 1 || bits > 8) return EXL3_E_BITS;
+    if (codebook < 0 || codebook > 2) return EXL3_E_CODEBOOK;
+    if (out_dtype != EXL3_F16 && out_dtype != EXL3_BF16 && out_dtype != EXL3_F32) return EXL3_E_DTYPE;
+    if (!aligned(xh, 16) || !aligned(trellis, 16) || !aligned(y, 16) || !aligned(svh, 2) || !aligned(status, 4))
+        return EXL3_E_ALIGN;
+    if (int e = check_device()) return e;
+    auto encode = get_encode();
+    if (!encode) return EXL3_E_CUDA;
+
+    // xh: fp16 (M, k) row-major -> 2D map {k, M}, box {64, 256}, 128-byte swizzle, zero fill past M
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)kGemmBM};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(xh), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return EXL3_E_CUDA;
+
+    GemmParams prm{};
+    prm.trellis = trellis;
+    prm.svh = static_cast<const __half*>(svh);
+    prm.y = y;
+    prm.status = status;
+    prm.M = M;
+    prm.k = k;
+    prm.n = n;
+    prm.KT = k / 16;
+    prm.NT = n / 16;
+    prm.out_dtype = out_dtype;
+    const dim3 grid(n / kGemmBN, (M + kGemmBM - 1) / kGemmBM);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (bits) {
+    case 1: return launch_gemm_cb<1>(codebook, map, prm, grid, s);
+    case 2: return launch_gemm_cb<2>(codebook, map, prm, grid, s);
+    case 3: return launch_gemm_cb<3>(codebook, map, prm, grid, s);
+    case 4: return launch_gemm_cb<4>(codebook, map, prm, grid, s);
+    case 5: return launch_gemm_cb<5>(codebook, map, prm, grid, s);
+    case 6: return launch_gemm_cb<6>(codebook, map, prm, grid, s);
+    case 7: return launch_gemm_cb<7>(codebook, map, prm, grid, s);
+    default: return launch_gemm_cb<8>(codebook, map, prm, grid, s);
+    }
+}

@@ -169,3 +169,37 @@ def had_svh(y: torch.Tensor, svh: torch.Tensor, out_dtype: torch.dtype) -> torch
     check(lib().exl3_had_svh(y.data_ptr(), dtype_code(y.dtype), rows, n, svh.data_ptr(), out.data_ptr(),
                              dtype_code(out_dtype), stream_ptr(y.device)), "exl3_had_svh")
     return out
+
+
+_status_words: dict = {}
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    t = _status_words.get(device)
+    if t is None:
+        t = _status_words[device] = torch.zeros(4, dtype=torch.int32, device=device)
+    return t
+
+
+def gemm(xh: torch.Tensor, trellis_u32: torch.Tensor, k: int, n: int, K: int, cb: int, svh: torch.Tensor,
+         out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Prefill product with the trellis decoded in the kernel: out_dtype(had128(xh @ W) / sqrt(128) * svh)
+    for xh fp16 (M, k). Needs k % 64 == 0 and n % 128 == 0 (EXL3Linear._prefill, linear.py:97-105)."""
+    M = xh.shape[0]
+    _need_cuda(xh, trellis_u32, svh)
+    if xh.dtype != torch.float16:
+        raise TypeError("xh must be fp16")
+    if trellis_u32.numel() * trellis_u32.element_size() != k * n * K // 8:
+        raise ValueError(f"trellis holds {trellis_u32.numel() * trellis_u32.element_size()} bytes, "
+                         f"expected {k * n * K // 8} for {k}x{n} at {K} bpw")
+    xh = xh.contiguous()
+    svh = svh.to(torch.float16).reshape(-1).contiguous()
+    y = out if out is not None else torch.empty((M, n), dtype=out_dtype, device=xh.device)
+    check(lib().exl3_gemm(xh.data_ptr(), M, k, n, trellis_u32.data_ptr(), K, cb, svh.data_ptr(), y.data_ptr(),
+                          dtype_code(y.dtype), _status(xh.device).data_ptr(), stream_ptr(xh.device)), "exl3_gemm")
+    return y
+
+
+def gemm_status(device: torch.device | None = None) -> int:
+    """The prefill kernel's error word on `device` (0 = no bounded wait ever gave up)."""
+    return int(_status(device or torch.device("cuda", torch.cuda.current_device()))[0].item())

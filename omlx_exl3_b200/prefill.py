@@ -1,14 +1,15 @@
 """Prefill (rows > MAX_GEMV_ROWS) path of EXL3Linear (daig/omlx-exl3 src/omlx/exl3/linear.py:97-121).
 
-xh = rot(x, suh) (fp16, as the reference casts the activations to fp16 before rotating), the
-trellis decoded to fp16 W^T in column chunks (kernels.decode_wt, bit-exact), the fp16 product,
-then the output rotation and svh (kernels.had_svh).
+xh = rot(x, suh) in fp16 (the reference casts the activations to fp16 before rotating), then the fused
+tcgen05 kernel (kernels.gemm: trellis decoded into shared memory, tensor-core product, output rotation
+and svh in the epilogue). Shapes the fused kernel does not take (k % 64 != 0) decode W^T to fp16 in
+column chunks (kernels.decode_wt, bit-exact), multiply, and rotate with kernels.had_svh.
 """
 from __future__ import annotations
 
 import torch
 
-from .kernels import decode_wt, had_svh, rot
+from .kernels import decode_wt, gemm, had_svh, rot
 
 PREFILL_COL_CHUNK = 16384
 
@@ -18,6 +19,8 @@ def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, c
     """(rows, n) = had128(had128(x2 * suh) @ W) * svh for x2 (rows, k)."""
     rows = x2.shape[0]
     xh = rot(x2, suh.reshape(1, -1))[0]
+    if k % 64 == 0 and n % 128 == 0:
+        return gemm(xh, tr, k, n, K, cb, svh, out_dtype)
     y = torch.empty((rows, n), dtype=torch.float16, device=x2.device)
     for c0 in range(0, n, PREFILL_COL_CHUNK):
         c = min(PREFILL_COL_CHUNK, n - c0)
