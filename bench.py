@@ -314,6 +314,63 @@ def run_ours(args, rank, world, local_rank):
     return out
 
 
+# ------------------------------------------------------------------------------------------ prefill
+
+def run_prefill(args, local_rank):
+    """prefill GEMM at 6 bpw, M in {512, 4096} x (5120->17408, 17408->5120), bf16
+    output. The fused kernel (trellis decoded in shared memory, tcgen05 into tensor memory) and the
+    decode-once path (exl3_decode_wt to fp16, a library fp16 GEMM, exl3_had_svh) are both timed with
+    CUDA events; TFLOP/s counts 2*M*k*n."""
+    import torch
+
+    from omlx_exl3_b200 import kernels
+
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    _, tf_peak, kind = load_peaks()
+    rows = []
+    for (k, n) in ((5120, 17408), (17408, 5120)):
+        K = 6
+        tr = torch.randint(-2 ** 31, 2 ** 31 - 1, (k * n * K // 32,), dtype=torch.int32, device=dev, generator=gen)
+        svh = (torch.randint(0, 2, (n,), device=dev, generator=gen).to(torch.float16) * 2 - 1)
+        for M in (512, 4096):
+            xh = torch.randn((M, k), device=dev, generator=gen).to(torch.float16)
+            y = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
+            wt = torch.empty((n, k), dtype=torch.float16, device=dev)
+            yh = torch.empty((M, n), dtype=torch.float16, device=dev)
+
+            def fused():
+                kernels.gemm(xh, tr, k, n, K, 0, svh, torch.bfloat16, out=y)
+
+            def decode_once():
+                kernels.decode_wt(tr, k, n, K, 0, out=wt)
+                torch.matmul(xh, wt.t(), out=yh)
+                kernels.had_svh(yh, svh, torch.bfloat16)
+
+            res = {"M": M, "k": k, "n": n, "bits": K}
+            for name, fn in (("fused_tcgen05", fused), ("decode_once_gemm", decode_once)):
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize(dev)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                it = 10
+                a.record()
+                for _ in range(it):
+                    fn()
+                b.record()
+                torch.cuda.synchronize(dev)
+                ms = a.elapsed_time(b) / it
+                tf = 2.0 * M * k * n / (ms * 1e-3) / 1e12
+                res[name] = {"us": round(ms * 1000, 1), "TFLOPs": round(tf, 1), "frac": round(tf / tf_peak, 4)}
+            rows.append(res)
+            del xh, y, wt, yh
+        del tr
+    torch.cuda.empty_cache()
+    return {"peak_TFLOPs": tf_peak, "peak_kind": f"{kind} bf16 sustained (fp16 has the same rate)",
+            "status": kernels.gemm_status(dev), "cases": rows}
+
+
 # ------------------------------------------------------------------------------------------ decode
 
 def run_decode(args, rank, world, local_rank):
@@ -477,6 +534,7 @@ def main():
     ap.add_argument("--case", default=None, help="k,n,K,rows: one GEMV configuration instead of the sweep")
     ap.add_argument("--no-decode", action="store_true", help="skip the 27B-class TP decode measurement")
     ap.add_argument("--decode-layers", type=int, default=64)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
     args = ap.parse_args()
     select_case(args.case)
     args.warmup = max(args.warmup, 3)
@@ -500,9 +558,12 @@ def main():
     try:
         out = run_ours(args, rank, world, local_rank)
         dec = None if (args.no_decode or args.case) else run_decode(args, rank, world, local_rank)
+        pre = run_prefill(args, local_rank) if (world == 1 and not args.case and not args.no_prefill) else None
         if out is not None:
             if dec is not None:
                 out["decode"] = dec
+            if pre is not None:
+                out["prefill_gemm"] = pre
             if world == 1 and not args.no_cpu_baseline:
                 out["cpu_baseline"] = cpu_reference_sample(budget_s=12.0)
             print(json.dumps(out), flush=True)

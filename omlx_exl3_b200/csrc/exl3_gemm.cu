@@ -33,13 +33,14 @@ constexpr int kGemmBM = 256;                  // rows of xh per CTA (two M=128 M
 constexpr int kGemmBN = 128;                  // output columns per CTA
 constexpr int kGemmBK = 64;                   // k per pipeline stage (128 bytes of fp16: one swizzle row)
 constexpr int kGemmStages = 3;
-constexpr int kGemmDecWarps = 8;
+constexpr int kGemmDecWarps = 16;
 constexpr int kGemmThreads = 32 * (2 + kGemmDecWarps);
 constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;   // 32 KB
 constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;   // 16 KB
 constexpr int kGemmDecDepth = 4;              // trellis k-steps in flight per decoder warp
 // + per decoder warp a ring of kGemmDecDepth x 4 tiles x 32K bytes (K <= 8: 256 bytes per tile)
-constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmABytes + kGemmBBytes) + 256 + kGemmDecWarps * kGemmDecDepth * 4 * 256;
+constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmABytes + kGemmBBytes) + 256 + kGemmDecWarps * kGemmDecDepth * 2 * 256;
+static_assert(kGemmBM * 129 * 4 <= kGemmStages * (kGemmABytes + kGemmBBytes), "epilogue exchange buffer");
 
 struct GemmParams {
     const uint32_t* trellis;
@@ -140,10 +141,10 @@ __device__ __forceinline__ uint32_t pack_weights(uint32_t sa, uint32_t sb)
 }
 
 template <typename OT>
-__device__ __forceinline__ void store_row128(OT* dst, const float (&v)[128], const __half* svh)
+__device__ __forceinline__ void store_row64(OT* dst, const float (&v)[64], const __half* svh)
 {
 #pragma unroll
-    for (int c = 0; c < 128; c += 8) {
+    for (int c = 0; c < 64; c += 8) {
         if constexpr (sizeof(OT) == 4) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) dst[c + i] = from_f32<OT>(v[c + i] * kHadScale * __half2float(svh[c + i]));
@@ -245,9 +246,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         const int dw = warp - 2;                                // 0..7
         const int g = lane >> 2, q = lane & 3;
         const LaneWindow<K> lw(lane);
-        // warp dw decodes k-slice dw / 2 and the four n-tiles 4 * (dw % 2) .. +3 of every k-step
-        constexpr int kTiles = 4;
-        const int ktl = dw >> 1, nt_base = (dw & 1) * kTiles;
+        // warp dw decodes k-slice dw / 4 and the two n-tiles 2 * (dw % 4) + {0, 1} of every k-step
+        constexpr int kTiles = 2;
+        const int ktl = dw >> 2, nt_base = (dw & 3) * kTiles;
         // The warp's tiles of a k-step are contiguous (kTiles * TW words); they are streamed into a
         // private ring of kGemmDecDepth slots with cp.async, kGemmDecDepth - 1 steps ahead.
         uint32_t* dring = reinterpret_cast<uint32_t*>(Bs + kGemmStages * kGemmBBytes + 256) +
@@ -306,39 +307,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         }
         cp_async_wait<0>();                                     // no copy in flight past this point
 
-        // ---- epilogue: one accumulator row per thread
-        const int h = dw >> 2;                                  // M half
+        // ---- epilogue: each thread takes 64 columns of one accumulator row; the 16 decoder warps
+        // cover (M half, column half) x the 4 TMEM lane quarters
+        const int j = dw >> 2;                                  // 0..3
+        const int h = j >> 1, chalf = j & 1;
         const int quarter = warp & 3;                           // TMEM lanes this warp may access
-        const int row = m0 + h * 128 + quarter * 32 + lane;
+        const int rloc = h * 128 + quarter * 32 + lane;         // row inside the CTA tile
+        const int row = m0 + rloc;
         const bool done = mbar_wait(accum, 0);
         if (!done) atomicOr(p.status, kStatusPipeTimeout);
         tc_fence_after();
-        float v[128];
-        const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN);
+        float v[64];
+        const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN + chalf * 64);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
             float part[32];
             tc_ld32(tbase + c * 32, part);
             tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[c * 32 + i] = part[i];
         }
-        if (done && row < p.M) {
+        // FWHT stages h = 1..32 stay inside a 64-column half
 #pragma unroll
-            for (int hs = 1; hs < 128; hs <<= 1) {
+        for (int hs = 1; hs < 64; hs <<= 1) {
 #pragma unroll
-                for (int b = 0; b < 64; ++b) {
-                    const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
-                    const float a0 = v[i0], a1 = v[i1];
-                    v[i0] = a0 + a1;
-                    v[i1] = a0 - a1;
-                }
+            for (int b = 0; b < 32; ++b) {
+                const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
+                const float a0 = v[i0], a1 = v[i1];
+                v[i0] = a0 + a1;
+                v[i1] = a0 - a1;
             }
-            const __half* sv = p.svh + (size_t)nb * kGemmBN;
-            const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN;
-            if (p.out_dtype == EXL3_F16) store_row128(static_cast<__half*>(p.y) + off, v, sv);
-            else if (p.out_dtype == EXL3_BF16) store_row128(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
-            else store_row128(static_cast<float*>(p.y) + off, v, sv);
+        }
+        // stage h = 64 pairs column c with c + 64: exchange halves through shared memory (the
+        // operand stages are free once every MMA has completed); rows padded to 129 floats
+        float* xbuf = reinterpret_cast<float*>(smem);
+        constexpr int kRow = 129;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) xbuf[rloc * kRow + chalf * 64 + i] = v[i];
+        named_bar_sync(1, 32 * kGemmDecWarps);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            const float other = xbuf[rloc * kRow + (chalf ^ 1) * 64 + i];
+            v[i] = chalf == 0 ? v[i] + other : other - v[i];
+        }
+        if (done && row < p.M) {
+            const __half* sv = p.svh + (size_t)nb * kGemmBN + chalf * 64;
+            const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN + chalf * 64;
+            if (p.out_dtype == EXL3_F16) store_row64(static_cast<__half*>(p.y) + off, v, sv);
+            else if (p.out_dtype == EXL3_BF16) store_row64(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
+            else store_row64(static_cast<float*>(p.y) + off, v, sv);
         }
     }
 

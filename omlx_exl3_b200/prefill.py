@@ -12,14 +12,20 @@ import torch
 from .kernels import decode_wt, gemm, had_svh, rot
 
 PREFILL_COL_CHUNK = 16384
+# Up to this many rows the fused kernel is the faster of the two (measured on B200 at the 27B-class
+# shapes: it decodes every weight once per 256 rows, which costs more than one fp16 round trip of W
+# through HBM once the row count is large).
+FUSED_MAX_ROWS = 1024
 
 
 def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, cb: int, suh: torch.Tensor,
-                   svh: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+                   svh: torch.Tensor, out_dtype: torch.dtype = torch.float32, fused: bool | None = None) -> torch.Tensor:
     """(rows, n) = had128(had128(x2 * suh) @ W) * svh for x2 (rows, k)."""
     rows = x2.shape[0]
     xh = rot(x2, suh.reshape(1, -1))[0]
-    if k % 64 == 0 and n % 128 == 0:
+    if fused is None:
+        fused = rows <= FUSED_MAX_ROWS
+    if fused and k % 64 == 0 and n % 128 == 0:
         return gemm(xh, tr, k, n, K, cb, svh, out_dtype)
     y = torch.empty((rows, n), dtype=torch.float16, device=x2.device)
     for c0 in range(0, n, PREFILL_COL_CHUNK):
