@@ -535,6 +535,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the 27B-class TP decode measurement")
     ap.add_argument("--decode-layers", type=int, default=64)
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the TP decode measurement (prints its own JSON line; for profiling the step)")
     args = ap.parse_args()
     select_case(args.case)
     args.warmup = max(args.warmup, 3)
@@ -556,6 +558,12 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:
+        if args.decode_only:
+            dec = run_decode(args, rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps({"metric": "decode_tok_s", "value": dec["tok_s"], "unit": "tok/s", "n_gpus": world,
+                                  "decode": dec}), flush=True)
+            return
         out = run_ours(args, rank, world, local_rank)
         dec = None if (args.no_decode or args.case) else run_decode(args, rank, world, local_rank)
         pre = run_prefill(args, local_rank) if (world == 1 and not args.case and not args.no_prefill) else None

@@ -151,6 +151,33 @@ EXL3_API int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* trel
 EXL3_API int exl3_had_svh(const void* y, int y_dtype, int rows, int n, const void* svh, void* out, int out_dtype,
                           void* stream);
 
+/*
+ * Decode-step attention glue after the fused q/k/v GEMV (head_dim 128, rotate-half RoPE):
+ *   q_out[r, h]           = fp16(T(rope(rms_norm(q[r, h]) * q_norm_w)))          for h < hq
+ *   k_cache[h, pos[r]]    = fp16(T(rope(rms_norm(k[r, h]) * k_norm_w)))          for h < hkv
+ *   v_cache[h, pos[r]]    = fp16(v[r, h])
+ * q/k/v rows of dtype T (EXL3_F16 / EXL3_BF16) with element strides q_stride/k_stride/v_stride between
+ * rows; norms round as mx.fast.rms_norm does. cos_table/sin_table: f32 (max_len, 64); pos: int64
+ * (rows); caches fp16 (hkv, max_len, 128); q_out fp16 (rows, hq, 128).
+ * Replaces: the q_norm / k_norm / RoPE / KV-cache update of the attention module the EXL3 q/k/v
+ * projections feed (the fused-norm consumer set of src/omlx/exl3/fusion.py:8-10; the attention
+ * module itself is the model library's, outside the reference tree). No counterpart kernel in the
+ * reference: there these are separate framework ops.
+ */
+EXL3_API int exl3_qkv_post(const void* q, const void* k, const void* v, int q_stride, int k_stride, int v_stride,
+                           int dtype, int rows, int hq, int hkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                           const float* cos_table, const float* sin_table, const long long* pos, void* k_cache,
+                           void* v_cache, int max_len, void* q_out, void* stream);
+
+/*
+ * Residual add fused into norm_rot: x_out = T(x + d); xn = T(w * T(x_out * rsqrt(mean(x_out^2) + eps)));
+ * xh[m] = fp16(had128(xn * suh[m]) / sqrt(128)). Replaces: `h = x + attn_out` followed by
+ * kernels.norm_rot (src/omlx/exl3/kernels.py:408-425, :461-473). x_out must not alias x or d
+ * (every block of a row reads the whole row); k % 128 == 0; suh fp16 (n_members, k).
+ */
+EXL3_API int exl3_add_norm_rot(const void* x, const void* d, const void* w, int dtype, int rows, int k, float eps,
+                               const void* suh, int n_members, void* x_out, void* xn, void* xh, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -171,6 +171,58 @@ def had_svh(y: torch.Tensor, svh: torch.Tensor, out_dtype: torch.dtype) -> torch
     return out
 
 
+def _rows_view(t: torch.Tensor, width: int) -> int:
+    """Row stride (elements) of a (rows, width) view whose elements are contiguous within a row."""
+    assert t.dim() == 2 and t.shape[1] == width and t.stride(1) == 1, "need (rows, width) with unit column stride"
+    return t.stride(0)
+
+
+def qkv_post(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
+             eps: float, cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor, k_cache: torch.Tensor,
+             v_cache: torch.Tensor, q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-head q/k RMSNorm + rotate-half RoPE, k/v into the fp16 caches at pos; returns q fp16 (rows, hq, 128).
+
+    q (rows, hq*128), k and v (rows, hkv*128) in one dtype (views into a fused projection output are
+    fine); cos/sin f32 (max_len, 64); pos int64 (rows); caches fp16 (hkv, max_len, 128).
+    """
+    rows = q.shape[0]
+    hq, hkv = q.shape[1] // 128, k.shape[1] // 128
+    max_len = k_cache.shape[1]
+    _need_cuda(q, k, v, k_cache, v_cache)
+    assert q.dtype == k.dtype == v.dtype and k_cache.dtype == v_cache.dtype == torch.float16
+    assert k_cache.is_contiguous() and v_cache.is_contiguous() and tuple(k_cache.shape) == (hkv, max_len, 128)
+    assert cos.dtype == sin.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous()
+    assert cos.shape[1] == 64 and pos.dtype == torch.int64 and pos.is_contiguous()
+    sq, sk, sv = _rows_view(q, hq * 128), _rows_view(k, hkv * 128), _rows_view(v, hkv * 128)
+    if q_out is None:
+        q_out = torch.empty((rows, hq, 128), dtype=torch.float16, device=q.device)
+    check(lib().exl3_qkv_post(q.data_ptr(), k.data_ptr(), v.data_ptr(), sq, sk, sv, dtype_code(q.dtype), rows, hq, hkv,
+                              q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(),
+                              pos.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), max_len, q_out.data_ptr(),
+                              stream_ptr(q.device)), "exl3_qkv_post")
+    return q_out
+
+
+def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float,
+                 suh: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """h = x + d, RMSNorm(h) * w (MLX rounding) and its rotations: returns (h, xn, xh (NM, rows, K) fp16)."""
+    rows, k = x.shape
+    suh = suh.reshape(-1, k)
+    nm = suh.shape[0]
+    assert k % 128 == 0 and x.dtype in (torch.bfloat16, torch.float16) and d.dtype == x.dtype
+    _need_cuda(x, d, w, suh)
+    x, d = x.contiguous(), d.contiguous()
+    w = w.to(x.dtype).contiguous()
+    suh = suh.to(torch.float16).contiguous()
+    h = torch.empty_like(x)
+    xn = torch.empty_like(x)
+    xh = torch.empty((nm, rows, k), dtype=torch.float16, device=x.device)
+    check(lib().exl3_add_norm_rot(x.data_ptr(), d.data_ptr(), w.data_ptr(), dtype_code(x.dtype), rows, k, float(eps),
+                                  suh.data_ptr(), nm, h.data_ptr(), xn.data_ptr(), xh.data_ptr(),
+                                  stream_ptr(x.device)), "exl3_add_norm_rot")
+    return h, xn, xh
+
+
 _status_words: dict = {}
 
 

@@ -170,7 +170,10 @@ def _finish(model: Qwen3EXL3, fuse: bool) -> Qwen3EXL3:
             m.reset_runtime()
     cast = unify_float_dtypes(model)
     groups = group_siblings(model)
-    fused = fuse_decode(model) if fuse and os.environ.get("OMLX_EXL3_FUSE", "1") != "0" else {}
+    fuse = fuse and os.environ.get("OMLX_EXL3_FUSE", "1") != "0"
+    fused = fuse_decode(model) if fuse else {}
+    model.fused_decode = fuse        # the fused decode step of Qwen3EXL3 (rows <= MAX_GEMV_ROWS)
+    model.reset_decode_plans()
     logger.info("EXL3: %d sibling groups, %d float tensors cast, fused rotations %s", groups, cast, fused)
     return model
 

@@ -22,6 +22,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
+from .kernels import MAX_GEMV_ROWS, add_norm_rot, norm_rot, qkv_post, rot, swiglu_rot
 from .linear import EXL3Linear
 
 
@@ -215,6 +216,59 @@ class DecoderLayer(nn.Module):
         return h + self.tp.all_reduce(self.mlp(self.post_attention_layernorm(h)))
 
 
+def _consumer_of(lin: EXL3Linear):
+    return lin._group if lin._group is not None else lin
+
+
+class _Targets:
+    """The distinct EXL3 consumers (sibling groups or single linears) of one normalised input, with
+    their stacked input scales: one rotation kernel writes all their rotated inputs."""
+
+    def __init__(self, linears: list[EXL3Linear]):
+        self.units = []
+        for lin in linears:
+            c = _consumer_of(lin)
+            if all(c is not u for u in self.units):
+                self.units.append(c)
+        self.nms = [u.rot_suh.shape[0] for u in self.units]
+        self.suh = torch.cat([u.rot_suh for u in self.units]).contiguous()
+
+    def outputs(self, xh: torch.Tensor, rows: int, out_dtype: torch.dtype) -> list[torch.Tensor]:
+        """Every unit's GEMV output from the stacked rotations xh (sum(nms), rows, k)."""
+        outs, o = [], 0
+        for u, nm in zip(self.units, self.nms):
+            if isinstance(u, EXL3Linear):
+                outs.append(u.gemv_rotated(xh[o:o + nm], out_dtype))
+            else:
+                outs.append(u.plan(rows, out_dtype)(xh[o:o + nm], u.trs))
+            o += nm
+        return outs
+
+
+class _LayerDecode:
+    """Per-layer state of the fused decode step (rows <= MAX_GEMV_ROWS)."""
+
+    def __init__(self, layer: DecoderLayer):
+        a, m = layer.self_attn, layer.mlp
+        self.qkv = _Targets([a.q_proj, a.k_proj, a.v_proj])
+        self.gate_up = _Targets([m.gate_proj, m.up_proj])
+        # column slices of each projection inside the unit outputs: (unit index, column offset, width)
+        self.qkv_at = [self._locate(self.qkv, lin) for lin in (a.q_proj, a.k_proj, a.v_proj)]
+        self.gu_at = [self._locate(self.gate_up, lin) for lin in (m.gate_proj, m.up_proj)]
+
+    @staticmethod
+    def _locate(t: _Targets, lin: EXL3Linear) -> tuple[int, int, int]:
+        c = _consumer_of(lin)
+        ui = next(i for i, u in enumerate(t.units) if u is c)
+        off = sum(c.ns[:lin._idx]) if c is not lin else 0
+        return ui, off, lin.out_features
+
+
+def _cols(outs: list[torch.Tensor], at: tuple[int, int, int]) -> torch.Tensor:
+    ui, off, n = at
+    return outs[ui][:, off:off + n]
+
+
 class Inner(nn.Module):
     def __init__(self, cfg: ModelConfig, tp: TP, layer_bits: list[dict], device):
         super().__init__()
@@ -253,8 +307,89 @@ class Qwen3EXL3(nn.Module):
         return self.model.norm(x)
 
     def forward(self, tokens: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        if tokens.shape[0] <= MAX_GEMV_ROWS and self.fused_decode and self._decode_ready():
+            return self._forward_decode(tokens, cache, pos)
         h = self.hidden(tokens, cache, pos)
         return self.lm_head(h) if self.lm_head is not None else h
+
+    # -- fused decode step ----------------------------------------------------------------------
+    # rows <= MAX_GEMV_ROWS: per layer  [add+]norm+rotate -> q/k/v GEMV -> qkv_post (q/k norm, RoPE,
+    # cache write) -> attention -> rotate -> o GEMV -> all-reduce -> add+norm+rotate -> gate/up GEMV ->
+    # SwiGLU+rotate -> down GEMV -> all-reduce; the MLP residual add is folded into the next layer's
+    # input norm (and the last one into the final norm). Same arithmetic and roundings as the module
+    # path above (the residual sums round to the model dtype in both).
+    fused_decode = True
+
+    def _decode_ready(self) -> bool:
+        plans = self.__dict__.get("_decode_plans")
+        if plans is None:
+            cfg = self.cfg
+            ok = (cfg.head_dim == 128 and cfg.hidden_size % 1024 == 0
+                  and cfg.dtype in (torch.float16, torch.bfloat16)
+                  and all(isinstance(getattr(l.self_attn, n), EXL3Linear) for l in self.model.layers
+                          for n in ("q_proj", "k_proj", "v_proj", "o_proj"))
+                  and all(isinstance(getattr(l.mlp, n), EXL3Linear) and "bias" not in getattr(l.mlp, n)
+                          for l in self.model.layers for n in ("gate_proj", "up_proj", "down_proj"))
+                  and all("bias" not in getattr(l.self_attn, n) for l in self.model.layers
+                          for n in ("q_proj", "k_proj", "v_proj", "o_proj")))
+            plans = [_LayerDecode(l) for l in self.model.layers] if ok else []
+            self.__dict__["_decode_plans"] = plans
+            self.__dict__["_head_targets"] = _Targets([self.lm_head]) if ok and self.lm_head is not None else None
+        return bool(plans)
+
+    def reset_decode_plans(self):
+        """Drop the fused-decode plans (after regrouping siblings or replacing linears)."""
+        self.__dict__.pop("_decode_plans", None)
+
+    def _forward_decode(self, tokens: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        eps = cfg.rms_norm_eps
+        rows = tokens.shape[0]
+        dt = cfg.dtype
+        x = self.model.embed_tokens(tokens)
+        d = None
+        T = cache.length + rows
+        for i, (layer, lp) in enumerate(zip(self.model.layers, self.__dict__["_decode_plans"])):
+            attn = layer.self_attn
+            w_in = layer.input_layernorm.weight
+            if d is None:
+                _, xh = norm_rot(x, w_in, eps, lp.qkv.suh)
+            else:
+                x, _, xh = add_norm_rot(x, d, w_in, eps, lp.qkv.suh)
+            outs = lp.qkv.outputs(xh, rows, dt)
+            kc, vc = cache.k[i], cache.v[i]
+            q16 = qkv_post(_cols(outs, lp.qkv_at[0]), _cols(outs, lp.qkv_at[1]), _cols(outs, lp.qkv_at[2]),
+                           attn.q_norm.weight, attn.k_norm.weight, eps, self.rope_cos, self.rope_sin, pos, kc, vc)
+            o = self._attend(q16, kc, vc, T, rows)
+            a = attn.o_proj.gemv_rotated(rot(o, attn.o_proj.rot_suh), dt)
+            self.tp.all_reduce(a)
+            x, _, xh = add_norm_rot(x, a, layer.post_attention_layernorm.weight, eps, lp.gate_up.suh)
+            gu_outs = lp.gate_up.outputs(xh, rows, torch.float16)
+            gu = gu_outs[0] if len(gu_outs) == 1 else torch.cat(
+                [_cols(gu_outs, lp.gu_at[0]), _cols(gu_outs, lp.gu_at[1])], dim=1)
+            down = layer.mlp.down_proj
+            d = down.gemv_rotated(swiglu_rot(gu, down.rot_suh.reshape(-1)), dt)
+            self.tp.all_reduce(d)
+        w_out = self.model.norm.weight
+        head = self.__dict__["_head_targets"]
+        if head is None:
+            return add_norm_rot(x, d, w_out, eps, torch.ones((1, x.shape[1]), dtype=torch.float16,
+                                                              device=x.device))[1]
+        _, _, xh = add_norm_rot(x, d, w_out, eps, head.suh)
+        return head.outputs(xh, rows, dt)[0]
+
+    @staticmethod
+    def _attend(q16: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, T: int, rows: int) -> torch.Tensor:
+        """GQA attention of the new rows (causal among themselves) over cache[:T]: (rows, hq*128) fp16."""
+        hq = q16.shape[1]
+        qh = q16.transpose(0, 1)[None]                                   # (1, hq, rows, 128)
+        mask = None
+        if rows > 1:
+            i = torch.arange(rows, device=q16.device)[:, None]
+            j = torch.arange(T, device=q16.device)[None, :]
+            mask = (j <= (T - rows + i))[None, None]
+        o = F.scaled_dot_product_attention(qh, kc[None, :, :T], vc[None, :, :T], attn_mask=mask, enable_gqa=True)
+        return o[0].transpose(0, 1).reshape(rows, hq * 128)
 
     def gather_logits(self, local: torch.Tensor) -> torch.Tensor:
         """All ranks' logit shards -> (rows, vocab) on every rank."""

@@ -23,11 +23,17 @@ def _kl(ref_logits, logits):
     return O.kl_div(ref_logits, logits)
 
 
-@pytest.mark.parametrize("fuse", [True, False])
+MIXED_BITS = {"q_proj": 5, "k_proj": 6, "v_proj": 6, "o_proj": 5, "gate_proj": 6, "up_proj": 4, "down_proj": 6}
+
+
+@pytest.mark.parametrize("path", ["step", "step_mixed", "modules_fused", "modules_plain"])
 @pytest.mark.parametrize("rows", [1, 3])
-def test_decode_logits_kl(cuda, fuse, rows):
+def test_decode_logits_kl(cuda, path, rows):
+    """step: the fused decode step (Qwen3EXL3._forward_decode); step_mixed: the same with q alone and
+    gate/up in separate launches; modules_*: the per-module path with and without the norm/MLP fusions."""
     torch.manual_seed(0)
-    model = _small_model(cuda, fuse=fuse)
+    model = _small_model(cuda, fuse=path != "modules_plain", bits=MIXED_BITS if path == "step_mixed" else None)
+    model.fused_decode = path.startswith("step")
     cache = model.make_cache(512)
     cache.fill_random(200, seed=1)
     toks = torch.tensor([5, 77, 1999][:rows], device=cuda)
@@ -72,6 +78,22 @@ def test_decode_runner_graph_matches_eager(cuda):
         eager = model(torch.tensor([11], device=cuda), cache, torch.tensor([300], device=cuda))
     assert torch.equal(la, eager)
     assert int(a.item()) == int(eager.float().argmax(-1).item())
+
+
+def test_fused_step_matches_module_path(cuda):
+    """The fused decode step and the module path compute the same roundings: logits agree closely."""
+    model = _small_model(cuda, fuse=True)
+    cache = model.make_cache(512)
+    cache.fill_random(100, seed=6)
+    toks = torch.tensor([3, 9], device=cuda)
+    pos = torch.tensor([100, 101], device=cuda)
+    with torch.no_grad():
+        model.fused_decode = True
+        a = model(toks, cache, pos).float()
+        model.fused_decode = False
+        b = model(toks, cache, pos).float()
+    assert torch.allclose(a, b, rtol=2e-2, atol=2e-2)
+    assert torch.equal(a.argmax(-1), b.argmax(-1))
 
 
 def test_sibling_group_and_fusion_installed(cuda):
