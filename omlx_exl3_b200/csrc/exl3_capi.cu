@@ -1,5 +1,9 @@
 // C-ABI utilities: status strings, version, device queries.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+
+#include <mutex>
 
 #include "exl3_b200.h"
 #include "exl3_host.h"
@@ -32,6 +36,20 @@ int check_device()
 }
 
 }  // namespace exl3
+
+PFN_cuTensorMapEncodeTiled_v12000 exl3_get_tensormap_encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
 
 extern "C" const char* exl3_strerror(int status)
 {

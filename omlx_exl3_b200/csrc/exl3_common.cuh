@@ -137,16 +137,17 @@ __device__ __forceinline__ uint32_t lane_state(const Window96<K>& v)
     }
 }
 
-// ------------------------------------------------------------------------------ balanced hashing
-// The decode is bound by two SM pipes: the integer ALU pipe (shifts, masks, byte permutes, the
-// codebook's and/xor) and the FMA pipe (integer multiply-adds), each 16 lanes per scheduler per
-// cycle. hashes8() produces the eight raw codebook hashes h_j = s_j * mul + add of a lane with
-// the state extractions split between the two pipes:
-//   exact    a 16-bit window isolated with a one-op form where one exists (and 0xffff, a byte
-//            permute, a multiply-high for the ">> 16"), else shift + mask;
-//   junk     X = any 32-bit value whose low half is the state and J = X >> 16; then
-//            s * mul + add = X * mul + add - J * (mul << 16), all on the FMA pipe. J is another
-//            state of the same lane when 16 is a multiple of K, else one multiply-high.
+// ------------------------------------------------------------------------------ hashing
+// The decode is bound by instruction issue on two SM pipes: the integer ALU pipe (shifts, masks, byte
+// permutes, the codebook's and/xor) and the FMA pipe (integer multiply-adds, fp16 FMAs), each 16
+// lanes per scheduler per cycle. Per state the floor is one extraction (one or two ops), one IMAD
+// for the hash and one LOP3 for the codebook's and/xor. Two things keep it there (measured with
+// per-pipe instruction counters on B200):
+//   * the codebook constants live in registers the compiler cannot see through (HashRegs): as
+//     literals, one of them is re-materialised at every LOP3 / IMAD (one extra ALU op per weight,
+//     ~8 per tile);
+//   * every state is isolated exactly (mask, byte permute, multiply-high, funnel shift); folding the
+//     unmasked high bits into a correcting multiply-add costs more issue slots than it saves.
 __device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) { return __umulhi(a, b); }
 
 template <int SH>
@@ -166,69 +167,44 @@ __device__ __forceinline__ uint32_t state_exact(const uint32_t (&w)[3])
     }
 }
 
-// A 32-bit value whose low 16 bits are the state at SH. STREAM: its upper 16 bits must be the
-// following stream bits (the junk is then another state of the lane); otherwise any upper bits
-// do, and an in-word window is taken with a multiply-high on the FMA pipe.
-template <int SH, bool STREAM>
-__device__ __forceinline__ uint32_t state_loose(const uint32_t (&w)[3])
-{
-    constexpr int wi = SH / 32, o = SH % 32;
-    if constexpr (o == 0) return w[wi];
-    else if constexpr (!STREAM && o + 16 <= 32) return mulhi(w[wi], 1u << (32 - o));
-    else return __funnelshift_r(w[wi], w[wi + 1], o);
-}
+// Codebook constants held in registers the compiler cannot see through (see above). They are read
+// from constant memory: a literal routed through an empty asm statement is still a literal to the
+// assembler, which then re-materialises it at each use.
+struct HashRegs {
+    uint32_t mul, add, msk, xr;
+};
+
+// [codebook][mul, add, and-mask, xor]
+static __constant__ uint32_t c_hash_consts[3][4] = {
+    {k3instMul, k3instAdd, 0x8fff8fffu, 0x3b603b60u},
+    {kMcgMul, 0u, 0x8fff8fffu, 0x3b603b60u},
+    {kMul1Mul, 0u, 0x8fff8fffu, 0x3b603b60u},
+};
 
 template <int CB>
-struct HashConst {
-    static constexpr uint32_t mul = CB == 0 ? k3instMul : (CB == 1 ? kMcgMul : kMul1Mul);
-    static constexpr uint32_t add = CB == 0 ? k3instAdd : 0u;
-    static constexpr uint32_t corr = 0u - (mul << 16);   // -(mul * 2^16) mod 2^32
-};
-
-// Which of the 8 states go through the junk form (bit j set), per bitrate. Chosen so that the
-// ALU and FMA instruction counts of a tile come out about equal (see the calibration notes in the
-// design document); the other states are extracted exactly.
-template <int K>
-struct JunkPlan {
-    static constexpr unsigned mask = K == 4 ? 0x80u : K == 8 ? 0x98u : K == 7 ? 0x60u : K == 6 ? 0x60u
-                                     : K == 5 ? 0x60u : K == 3 ? 0x30u : 0x00u;
-};
-
-template <int K, int CB>
-__device__ __forceinline__ void hashes8(const uint32_t (&w)[3], uint32_t (&h)[8])
+__device__ __forceinline__ HashRegs hash_regs()
 {
-    using C = HashConst<CB>;
-    constexpr unsigned JM = JunkPlan<K>::mask;
-    uint32_t s[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j] = 0;
-    // exact states first (they may serve as the junk of later states)
-#define EXL3_EXACT(J)                                                     \
-    if constexpr (!(JM & (1u << J))) s[J] = state_exact<(7 - J) * K>(w);
-    EXL3_EXACT(0) EXL3_EXACT(1) EXL3_EXACT(2) EXL3_EXACT(3)
-    EXL3_EXACT(4) EXL3_EXACT(5) EXL3_EXACT(6) EXL3_EXACT(7)
-#undef EXL3_EXACT
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        if (!(JM & (1u << j))) h[j] = s[j] * C::mul + C::add;
-#define EXL3_JUNK(J)                                                                            \
-    if constexpr (JM & (1u << J)) {                                                             \
-        constexpr int SH = (7 - J) * K;                                                         \
-        constexpr bool kFromState = 16 % K == 0 && J >= 16 / K && !(JM & (1u << ((J - 16 / K) & 7))); \
-        const uint32_t X = state_loose<SH, kFromState>(w);                                      \
-        uint32_t Jv;                                                                            \
-        if constexpr (kFromState) Jv = s[(J - 16 / K) & 7];                                     \
-        else Jv = mulhi(X, 1u << 16);                                                           \
-        h[J] = X * C::mul + C::add + Jv * C::corr;                                              \
-    }
-    EXL3_JUNK(0) EXL3_JUNK(1) EXL3_JUNK(2) EXL3_JUNK(3)
-    EXL3_JUNK(4) EXL3_JUNK(5) EXL3_JUNK(6) EXL3_JUNK(7)
-#undef EXL3_JUNK
+    HashRegs r;
+    r.mul = c_hash_consts[CB][0];
+    r.add = c_hash_consts[CB][1];
+    r.msk = c_hash_consts[CB][2];
+    r.xr = c_hash_consts[CB][3];
+    return r;
+}
+
+// The eight raw codebook hashes h_j = s_j * mul + add of a lane (s_j the state of position j).
+template <int K, int CB>
+__device__ __forceinline__ void hashes8(const uint32_t (&w)[3], uint32_t (&h)[8], const HashRegs& hr)
+{
+#define EXL3_HASH(J) h[J] = state_exact<(7 - J) * K>(w) * hr.mul + hr.add;
+    EXL3_HASH(0) EXL3_HASH(1) EXL3_HASH(2) EXL3_HASH(3)
+    EXL3_HASH(4) EXL3_HASH(5) EXL3_HASH(6) EXL3_HASH(7)
+#undef EXL3_HASH
 }
 
 // hash -> split MMA word (see split_word)
 template <int CB>
-__device__ __forceinline__ uint32_t split_from_hash(uint32_t h)
+__device__ __forceinline__ uint32_t split_from_hash(uint32_t h, const HashRegs& hr)
 {
     if constexpr (CB == 2) {
         const uint32_t r = __dp4a(h, 0x01010101u, 0x6400u);
@@ -238,7 +214,7 @@ __device__ __forceinline__ uint32_t split_from_hash(uint32_t h)
         const __half2 w = __hfma2(rr, a, c);
         return *reinterpret_cast<const uint32_t*>(&w);
     } else {
-        return (h & 0x8fff8fffu) ^ 0x3b603b60u;
+        return (h & hr.msk) ^ hr.xr;
     }
 }
 
@@ -311,15 +287,28 @@ __device__ __forceinline__ uint64_t global_ns()
     return t;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `hint_ns` while the phase is pending
+// (no issue slots spent polling).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: gives up (returns false) once `limit_ns` of wall time has passed without the phase
 // completing, so a lost completion turns into an error status instead of a hung GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && global_ns() - t0 > limit_ns) return false;
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
     }
 }
 

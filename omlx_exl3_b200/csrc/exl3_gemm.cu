@@ -26,6 +26,7 @@
 #include "exl3_b200.h"
 #include "exl3_common.cuh"
 #include "exl3_host.h"
+#include "exl3_tc.cuh"
 
 namespace exl3 {
 
@@ -49,76 +50,6 @@ struct GemmParams {
     uint32_t* status;
     int M, k, n, KT, NT, out_dtype;
 };
-
-// ------------------------------------------------------------------------------ tcgen05 / TMA PTX
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem()
-{
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p)
-{
-    const uint64_t addr = smem_addr(p);
-    uint64_t d = (addr >> 4) & 0x3FFFull;          // start address
-    d |= (uint64_t)(16 >> 4) << 16;                // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset: next 8-row group
-    d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;                        // layout: 128B swizzle
-    return d;
-}
-
-// Instruction descriptor: fp16 A/B, fp32 D, both K-major, M x N.
-constexpr uint32_t idesc_f16_f32(int M, int N)
-{
-    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate)
-{
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
-}
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32])
-{
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------------------------ decode into B
 // Byte offset of (row n, k) inside a K-major 128B-swizzled tile whose rows are 128 bytes (64 fp16):
@@ -246,6 +177,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         const int dw = warp - 2;                                // 0..7
         const int g = lane >> 2, q = lane & 3;
         const LaneWindow<K> lw(lane);
+        const HashRegs hr = hash_regs<CB>();
         // warp dw decodes k-slice dw / 4 and the two n-tiles 2 * (dw % 4) + {0, 1} of every k-step
         constexpr int kTiles = 2;
         const int ktl = dw >> 2, nt_base = (dw & 3) * kTiles;
@@ -286,9 +218,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 const uint32_t* tile = stage_tiles + t * TW;
                 uint32_t w[3], hsh[8], a[8];
                 window_words<K>(tile, lw, w);
-                hashes8<K, CB>(w, hsh);
+                hashes8<K, CB>(w, hsh, hr);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) a[j] = split_from_hash<CB>(hsh[j]);
+                for (int j = 0; j < 8; ++j) a[j] = split_from_hash<CB>(hsh[j], hr);
                 // lane holds column g (positions 0..3) and g+8 (4..7) at k 2q, 2q+1, 2q+8, 2q+9
                 const int n_lo = ntl * 16 + g, n_hi = n_lo + 8;
                 const int kb = ktl * 32 + 4 * q;                // byte of k = 16*ktl + 2q in the 128-byte row
@@ -368,20 +300,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 }
 
 // ------------------------------------------------------------------------------ host
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
 template <int K, int CB>
 static int launch_gemm_k(const CUtensorMap& map, const GemmParams& prm, dim3 grid, cudaStream_t s)
 {
@@ -422,7 +340,7 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
     if (!aligned(xh, 16) || !aligned(trellis, 16) || !aligned(y, 16) || !aligned(svh, 2) || !aligned(status, 4))
         return EXL3_E_ALIGN;
     if (int e = check_device()) return e;
-    auto encode = get_encode();
+    auto encode = exl3_get_tensormap_encoder();
     if (!encode) return EXL3_E_CUDA;
 
     // xh: fp16 (M, k) row-major -> 2D map {k, M}, box {64, 256}, 128-byte swizzle, zero fill past M

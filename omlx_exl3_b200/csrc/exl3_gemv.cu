@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
 
     const int g = lane >> 2, q = lane & 3;
     const LaneWindow<K> lw(lane);
+    const HashRegs hr = hash_regs<CB>();
     const int rows = p.rows;
     const int b_first = (int)(u0 / KT), b_last = (int)((u1 - 1) / KT);
     const bool xlane = ROWS1 || g < rows;         // this lane carries a row of xh
@@ -200,9 +201,9 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             for (int j = 0; j < 8; ++j) {
                 uint32_t w[3], h[8], a[8];
                 window_words<K>(unit + j * S::TW, lw, w);
-                hashes8<K, CB>(w, h);
+                hashes8<K, CB>(w, h, hr);
 #pragma unroll
-                for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t]);
+                for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t], hr);
                 if constexpr (ROWS1) {
                     // columns g (positions 0..3) and g+8 (4..7); k 2q, 2q+1, 2q+8, 2q+9
                     const __half2 xe0 = *reinterpret_cast<const __half2*>(&be0);
@@ -326,6 +327,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
         __syncthreads();   // red is reused by the next segment
     }
 }
+
 
 // ---------------------------------------------------------------------------------------- host
 
