@@ -43,7 +43,7 @@ struct GemvParams {
     void* y;                 // (rows, n_total)
     float* partials;         // grid * J * 8 * 128
     uint32_t* counters;      // blocks, then one status word
-    int k, KT, rows, n_total, blocks, out_bf16, J, row_exact;
+    int k, KT, rows, n_total, blocks, out_bf16, J, row_exact, gran;
     long long units;
 };
 
@@ -118,29 +118,53 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
     const int cw = threadIdx.x >> 5;
     const int ctid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;
-    const long long U = p.units;
-    const long long u0 = cta_start(c, U, G), u1 = cta_start(c + 1, U, G);
+    // CTA ranges are whole granules of p.gran units (16 when k is a multiple of 256), so every block
+    // segment inside a CTA is a whole number of rounds of the NCW warps
+    const int gran = p.gran;
+    const long long U = p.units / gran;
+    const long long u0 = cta_start(c, U, G) * gran, u1 = cta_start(c + 1, U, G) * gran;
     const int n_units = (int)(u1 - u0);
     const int KT = p.KT;
+    const int rows = p.rows;
+    const int b_first = (int)(u0 / KT), b_last = (int)((u1 - 1) / KT);
 
     // Every warp streams its own units (CTA unit indices cw, cw + NCW, ...) into a private ring of
-    // DEPTH slots with 16-byte cp.async copies, DEPTH - 1 units ahead of the one it decodes.
-    uint32_t* wring = reinterpret_cast<uint32_t*>(smem) + (size_t)cw * S::DEPTH * S::UW;
-    int fi = cw;                                              // next unit index to fetch
-    int fb = (int)((u0 + fi) / KT), fkt = (int)(u0 + fi - (long long)fb * KT);
+    // DEPTH slots with 16-byte cp.async copies, DEPTH - 1 units ahead of the one it decodes. The
+    // source pointer (already offset by this lane's first chunk) advances by a fixed stride while
+    // the warp stays inside one 128-column block and is recomputed only when it moves to the next.
+    constexpr int kChunks = S::UB / 16;                               // 16-byte chunks per unit
+    constexpr int kPerLane = (kChunks + 31) / 32;
+    uint32_t* wring = reinterpret_cast<uint32_t*>(smem) + (size_t)cw * S::DEPTH * S::UW + lane * 4;
+    int fi = cw;                                                      // next unit index to fetch
+    int fb = 0, fkt = 0;
+    const uint32_t* fsrc = nullptr;
+    size_t fstep = 0;                                                 // words between k-slices NCW apart
+    auto fseek = [&]() {
+        const long long u = u0 + fi;
+        fb = (int)(u / KT);
+        fkt = (int)(u - (long long)fb * KT);
+        const int m = (p.nm > 1 && fb >= p.blk_off[1]) ? ((p.nm > 2 && fb >= p.blk_off[2]) ? 2 : 1) : 0;
+        const int ntm = m == 0 ? p.nt_member[0] : (m == 1 ? p.nt_member[1] : p.nt_member[2]);
+        const int off = m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]);
+        const uint32_t* base = m == 0 ? p.trellis[0] : (m == 1 ? p.trellis[1] : p.trellis[2]);
+        fsrc = base + ((size_t)fkt * ntm + (size_t)(fb - off) * 8) * S::TW + lane * 4;
+        fstep = (size_t)NCW * ntm * S::TW;
+    };
+    if (fi < n_units) fseek();
     int fslot = 0;
     auto fetch = [&]() {
         if (fi < n_units) {
-            const int m = (p.nm > 1 && fb >= p.blk_off[1]) ? ((p.nm > 2 && fb >= p.blk_off[2]) ? 2 : 1) : 0;
-            const uint32_t* src = p.trellis[m] +
-                                  ((size_t)fkt * p.nt_member[m] + (size_t)(fb - p.blk_off[m]) * 8) * S::TW;
             uint32_t* dst = wring + (size_t)fslot * S::UW;
 #pragma unroll
-            for (int cidx = lane; cidx < S::UB / 16; cidx += 32)
-                cp_async16(dst + cidx * 4, src + cidx * 4);
+            for (int cidx = 0; cidx < kPerLane; ++cidx)
+                if (kChunks % 32 == 0 || cidx * 32 + lane < kChunks) cp_async16(dst + cidx * 128, fsrc + cidx * 128);
             fi += NCW;
             fkt += NCW;
-            while (fkt >= KT) { fkt -= KT; ++fb; }
+            if (fkt >= KT) {
+                if (fi < n_units) fseek();
+            } else {
+                fsrc += fstep;
+            }
         }
         cp_async_commit();                                    // (possibly empty) group per unit
         fslot = fslot + 1 == S::DEPTH ? 0 : fslot + 1;
@@ -152,8 +176,6 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
     const int g = lane >> 2, q = lane & 3;
     const LaneWindow<K> lw(lane);
     const HashRegs hr = hash_regs<CB>();
-    const int rows = p.rows;
-    const int b_first = (int)(u0 / KT), b_last = (int)((u1 - 1) / KT);
     const bool xlane = ROWS1 || g < rows;         // this lane carries a row of xh
 
     for (int b = b_first; b <= b_last; ++b) {
@@ -176,16 +198,16 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
         const int kt_base = (int)(u0 - (long long)b * KT);     // k-slice of unit index 0 (may be < 0)
         int i = sa + ((cw - sa) % NCW + NCW) % NCW;
         // the lane's xh values for the next unit are fetched one unit ahead
+        const __half* xp = xrow + (kt_base + i) * 16 + 2 * q;
         uint32_t x0n = 0, x1n = 0;
         if (i < se && xlane) {
-            const __half* xp = xrow + (kt_base + i) * 16 + 2 * q;
             x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
             x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
         }
         for (; i < se; i += NCW) {
             const uint32_t x0 = x0n, x1 = x1n;
+            xp += NCW * 16;
             if (i + NCW < se && xlane) {
-                const __half* xp = xrow + (kt_base + i + NCW) * 16 + 2 * q;
                 x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
                 x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
             }
@@ -195,7 +217,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             fetch();                                  // unit + DEPTH - 1 (or an empty group)
             cp_async_wait<S::DEPTH - 1>();            // this unit's copies have landed
             __syncwarp();
-            const uint32_t* unit = wring + (size_t)cslot * S::UW;
+            const uint32_t* unit = wring - lane * 4 + (size_t)cslot * S::UW;
             cslot = cslot + 1 == S::DEPTH ? 0 : cslot + 1;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -286,8 +308,8 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
                 __threadfence();
                 __syncwarp();
                 if (lane == 0) {
-                    const int c_first = owner_cta((long long)b * KT, U, G);
-                    const int c_last = owner_cta((long long)(b + 1) * KT - 1, U, G);
+                    const int c_first = owner_cta((long long)b * KT / gran, U, G);
+                    const int c_last = owner_cta(((long long)(b + 1) * KT - 1) / gran, U, G);
                     const unsigned old = atomicAdd(&p.counters[b], 1u);
                     const int last = old == (unsigned)(c_last - c_first);
                     if (last) __threadfence();
@@ -297,12 +319,12 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             __syncthreads();
             finish = s_last != 0;
             if (finish) {
-                const int c_first = owner_cta((long long)b * KT, U, G);
-                const int c_last = owner_cta((long long)(b + 1) * KT - 1, U, G);
+                const int c_first = owner_cta((long long)b * KT / gran, U, G);
+                const int c_last = owner_cta(((long long)(b + 1) * KT - 1) / gran, U, G);
                 for (int e = ctid; e < rows * 128; e += 32 * NCW) {
                     float v = 0.f;
                     for (int cc = c_first; cc <= c_last; ++cc) {
-                        const int jj = cc == c_first ? b - (int)(cta_start(cc, U, G) / KT) : 0;
+                        const int jj = cc == c_first ? b - (int)(cta_start(cc, U, G) * gran / KT) : 0;
                         v += __ldcg(p.partials + ((size_t)cc * p.J + jj) * kRedStride + e);
                     }
                     red[e] = v;
@@ -334,9 +356,49 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
 constexpr int kNCW = 16;
 
 struct GemvLaunch {
-    int grid, J, blocks, KT;
+    int grid, J, blocks, KT, gran;
     long long units;
 };
+
+// Grid choice. A CTA's time is about its unit count plus a fixed cost per block segment it ends
+// (the CTA-wide reduction; more when the block is split over CTAs: publish, fence, arrival ticket,
+// the last arriver's sum). Measured on B200 at the 27B-class shapes, one segment end costs about
+// as much as decoding 15 units, a split one about 45. Candidates: one CTA per SM, and grids that
+// split every block evenly (s CTAs per block) or give every CTA d whole blocks.
+static long long grid_cost(int blocks, int KT, int gran, long long G)
+{
+    constexpr long long kWholeEnd = 15, kSplitEnd = 45;
+    const long long U = (long long)blocks * KT / gran;
+    long long worst = 0;
+    for (long long c = 0; c < G; ++c) {
+        const long long u0 = c * U / G * gran, u1 = (c + 1) * U / G * gran;
+        if (u1 <= u0) continue;
+        long long cost = u1 - u0;
+        for (long long b = u0 / KT; b * KT < u1; ++b) {
+            const bool whole = b * KT >= u0 && (b + 1) * KT <= u1;
+            cost += whole ? kWholeEnd : kSplitEnd;
+        }
+        worst = cost > worst ? cost : worst;
+    }
+    return worst;
+}
+
+static int pick_grid(int blocks, int KT, int gran, int sms)
+{
+    long long best_g = sms, best = grid_cost(blocks, KT, gran, sms);
+    auto consider = [&](long long g) {
+        if (g < 1 || g > sms || g == best_g) return;
+        const long long c = grid_cost(blocks, KT, gran, g);
+        if (c < best) { best = c; best_g = g; }
+    };
+    if (blocks <= sms) {
+        for (int sp = sms / blocks; sp >= 1 && sp * blocks * 2 > sms; --sp) consider((long long)sp * blocks);
+    } else {
+        for (int dd = 2; dd <= 8; ++dd)
+            if (blocks % dd == 0) consider(blocks / dd);
+    }
+    return (int)best_g;
+}
 
 static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
 {
@@ -354,10 +416,12 @@ static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
     L->blocks = blocks;
     L->KT = d->k / 16;
     L->units = (long long)blocks * L->KT;
-    long long G = d->grid > 0 ? d->grid : device_sm_count();
-    if (G > L->units) G = L->units;
+    L->gran = L->KT % kNCW == 0 ? kNCW : 1;
+    const long long granules = L->units / L->gran;
+    long long G = d->grid > 0 ? d->grid : pick_grid(blocks, L->KT, L->gran, device_sm_count());
+    if (G > granules) G = granules;
     L->grid = (int)G;
-    const long long per = (L->units + G - 1) / G;
+    const long long per = (granules + G - 1) / G * L->gran;
     L->J = (int)((per + L->KT - 1) / L->KT + 1);
     return EXL3_OK;
 }
@@ -457,6 +521,7 @@ extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint3
     prm.J = L.J;
     prm.row_exact = (desc->flags & EXL3_GEMV_ROW_EXACT) != 0;
     prm.units = L.units;
+    prm.gran = L.gran;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (desc->bits) {
