@@ -434,12 +434,18 @@ def run_decode(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     runner.release()
+    peer_ar = model.tp.peers is not None
+    if world > 1:
+        barrier()
+    model.close_peers()
     weights = sum(b.numel() * b.element_size() for m in model.modules() for nm, b in m.named_buffers(recurse=False)
                   if nm == "trellis")
     del runner, model, cache
     torch.cuda.empty_cache()
     ms, ms_e2e = float(vals[0]), float(vals[1])
     return {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 4), "tp": world, "steps": n,
+            "allreduce": "fused NVLink peer kernel (exl3_ar_add_norm_rot)" if peer_ar else
+                         ("NCCL" if world > 1 else "none"),
             "e2e_tok_s": round(1000.0 / ms_e2e, 2),
             "trellis_bytes_per_gpu": int(weights),
             "weight_stream_GBps_per_gpu": round(weights / (ms * 1e-3) / 1e9, 1),

@@ -178,6 +178,47 @@ EXL3_API int exl3_qkv_post(const void* q, const void* k, const void* v, int q_st
 EXL3_API int exl3_add_norm_rot(const void* x, const void* d, const void* w, int dtype, int rows, int k, float eps,
                                const void* suh, int n_members, void* x_out, void* xn, void* xh, void* stream);
 
+/*
+ * Tensor-parallel peer buffers (CUDA IPC over NVLink). Each rank of a tensor-parallel group creates
+ * one buffer with exl3_peer_create (the one entry point that allocates device memory: the buffer
+ * must be its own cudaMalloc allocation to be shared), sends the 64-byte handle to the other ranks
+ * (any host transport), and maps theirs with exl3_peer_open. exl3_peer_close / exl3_peer_destroy
+ * undo the two. No counterpart in the reference (one Apple GPU); they carry the fused all-reduce.
+ */
+#define EXL3_PEER_HANDLE_BYTES 64
+EXL3_API int exl3_peer_create(size_t bytes, void** ptr, void* handle);
+EXL3_API int exl3_peer_destroy(void* ptr);
+EXL3_API int exl3_peer_open(const void* handle, void** ptr);
+EXL3_API int exl3_peer_close(void* ptr);
+
+/* One tensor-parallel group as seen by one rank. Buffer layout (byte offsets, same on every rank):
+ * a 64-byte flag block at flag_off (zeroed at creation), and two partial slots of slot_bytes at
+ * data_off and data_off + slot_bytes. */
+typedef struct exl3_peer_group {
+    int32_t world;           /* 1..8 */
+    int32_t rank;            /* this process's rank */
+    void* base[8];           /* every rank's buffer as mapped in this process (base[rank] = own) */
+    uint64_t flag_off;       /* multiple of 64 */
+    uint64_t data_off;       /* multiple of 16 */
+    uint64_t slot_bytes;     /* multiple of 16, >= rows * k * 2 */
+} exl3_peer_group;
+
+/*
+ * All-reduce of the row-parallel partials fused with residual add + RMSNorm + input rotation:
+ *   d = sum over ranks (in rank order, fp32) of slot `slot` of every rank's buffer, (rows, k) of dtype T,
+ *   then exactly exl3_add_norm_rot(x, T(d), w, ...). The caller's GEMV must have written this rank's
+ *   partial into its own slot `slot`; consecutive calls alternate slot 0 / 1; every rank makes the
+ *   same sequence of calls. Waits for the other ranks' flags at most 2 s, then sets a status bit
+ *   (exl3_peer_status) and continues. Replaces: the NCCL all-reduce + exl3_add_norm_rot pair of the
+ *   tensor-parallel decode step (the reference runs on one GPU; its norm-rotation is
+ *   src/omlx/exl3/kernels.py:408-425). k % 128 == 0, k <= 16384, rows <= 8.
+ */
+EXL3_API int exl3_ar_add_norm_rot(const exl3_peer_group* g, int slot, const void* x, const void* w, int dtype,
+                                  int rows, int k, float eps, const void* suh, int n_members, void* x_out,
+                                  void* xn, void* xh, void* stream);
+/* Status bits of the group's own flag block (4 = a wait for another rank timed out). */
+EXL3_API int exl3_peer_status(const exl3_peer_group* g, uint32_t* status);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,15 @@ class GemvDesc(ctypes.Structure):
 GEMV_ROW_EXACT = 1
 
 
+class PeerGroupDesc(ctypes.Structure):
+    """exl3_peer_group: one tensor-parallel group as seen by one rank."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("base", ctypes.c_void_p * 8),
+                ("flag_off", ctypes.c_uint64), ("data_off", ctypes.c_uint64), ("slot_bytes", ctypes.c_uint64)]
+
+
+PEER_HANDLE_BYTES = 64
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -58,6 +67,13 @@ SIGNATURES = {
     "exl3_gemm": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _P, _I, _P, _P]),
     "exl3_qkv_post": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _P, _P, _I, _P, _P]),
     "exl3_add_norm_rot": (_I, [_P, _P, _P, _I, _I, _I, _F, _P, _I, _P, _P, _P, _P]),
+    "exl3_peer_create": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "exl3_peer_destroy": (_I, [_P]),
+    "exl3_peer_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "exl3_peer_close": (_I, [_P]),
+    "exl3_ar_add_norm_rot": (_I, [ctypes.POINTER(PeerGroupDesc), _I, _P, _P, _I, _I, _I, _F, _P, _I, _P, _P, _P,
+                                  _P]),
+    "exl3_peer_status": (_I, [ctypes.POINTER(PeerGroupDesc), ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 

@@ -8,6 +8,8 @@ inside the same graph.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .model import KVCache, Qwen3EXL3
@@ -23,6 +25,8 @@ class DecodeRunner:
         self.next_tokens = None
         self.logits = None
         self.graph = None
+        if os.environ.get("OMLX_EXL3_PEER_AR", "1") != "0":
+            model.setup_peers(rows)      # tensor-parallel: fused NVLink all-reduce (collective)
         self._run()                      # eager pass: builds GEMV plans and their scratch
         torch.cuda.synchronize(dev)
         if use_graph:

@@ -64,6 +64,7 @@ class TP:
     rank: int = 0
     size: int = 1
     group: object = None
+    peers: object = None      # comm.PeerGroup once setup_peers() ran: fused NVLink all-reduce
 
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.size > 1:
@@ -346,37 +347,67 @@ class Qwen3EXL3(nn.Module):
         eps = cfg.rms_norm_eps
         rows = tokens.shape[0]
         dt = cfg.dtype
+        hs = cfg.hidden_size
+        peers = self.tp.peers if self.tp.size > 1 else None
         x = self.model.embed_tokens(tokens)
-        d = None
         T = cache.length + rows
+        pending = None          # the row-parallel output still to be summed over ranks and added to x
+        slot = 0                # peer-buffer slot of the next row-parallel output (alternates)
+
+        def row_parallel(lin: EXL3Linear, xh_in: torch.Tensor):
+            nonlocal slot
+            if peers is None:
+                return self.tp.all_reduce(lin.gemv_rotated(xh_in, dt))
+            out = peers.slot_view(slot, rows, hs, dt)
+            lin.plan(rows, dt)(xh_in, [lin._tr], out=out)
+            slot ^= 1
+            return slot ^ 1
+
+        def add_norm(x, pend, w, suh):
+            if peers is None:
+                return add_norm_rot(x, pend, w, eps, suh)
+            return peers.ar_add_norm_rot(pend, x, w, eps, suh)
+
         for i, (layer, lp) in enumerate(zip(self.model.layers, self.__dict__["_decode_plans"])):
             attn = layer.self_attn
             w_in = layer.input_layernorm.weight
-            if d is None:
+            if pending is None:
                 _, xh = norm_rot(x, w_in, eps, lp.qkv.suh)
             else:
-                x, _, xh = add_norm_rot(x, d, w_in, eps, lp.qkv.suh)
+                x, _, xh = add_norm(x, pending, w_in, lp.qkv.suh)
             outs = lp.qkv.outputs(xh, rows, dt)
             kc, vc = cache.k[i], cache.v[i]
             q16 = qkv_post(_cols(outs, lp.qkv_at[0]), _cols(outs, lp.qkv_at[1]), _cols(outs, lp.qkv_at[2]),
                            attn.q_norm.weight, attn.k_norm.weight, eps, self.rope_cos, self.rope_sin, pos, kc, vc)
             o = self._attend(q16, kc, vc, T, rows)
-            a = attn.o_proj.gemv_rotated(rot(o, attn.o_proj.rot_suh), dt)
-            self.tp.all_reduce(a)
-            x, _, xh = add_norm_rot(x, a, layer.post_attention_layernorm.weight, eps, lp.gate_up.suh)
+            a = row_parallel(attn.o_proj, rot(o, attn.o_proj.rot_suh))
+            x, _, xh = add_norm(x, a, layer.post_attention_layernorm.weight, lp.gate_up.suh)
             gu_outs = lp.gate_up.outputs(xh, rows, torch.float16)
             gu = gu_outs[0] if len(gu_outs) == 1 else torch.cat(
                 [_cols(gu_outs, lp.gu_at[0]), _cols(gu_outs, lp.gu_at[1])], dim=1)
             down = layer.mlp.down_proj
-            d = down.gemv_rotated(swiglu_rot(gu, down.rot_suh.reshape(-1)), dt)
-            self.tp.all_reduce(d)
+            pending = row_parallel(down, swiglu_rot(gu, down.rot_suh.reshape(-1)))
         w_out = self.model.norm.weight
         head = self.__dict__["_head_targets"]
         if head is None:
-            return add_norm_rot(x, d, w_out, eps, torch.ones((1, x.shape[1]), dtype=torch.float16,
-                                                              device=x.device))[1]
-        _, _, xh = add_norm_rot(x, d, w_out, eps, head.suh)
+            return add_norm(x, pending, w_out, torch.ones((1, hs), dtype=torch.float16, device=x.device))[1]
+        _, _, xh = add_norm(x, pending, w_out, head.suh)
         return head.outputs(xh, rows, dt)[0]
+
+    def close_peers(self):
+        """Release the peer buffers (every rank, after the last decode step of the group)."""
+        if self.tp.peers is not None:
+            self.tp.peers.close()
+            self.tp.peers = None
+
+    def setup_peers(self, max_rows: int = MAX_GEMV_ROWS):
+        """Collective over the tensor-parallel group: map the ranks' NVLink peer buffers so the decode
+        step sums row-parallel outputs with the fused all-reduce kernel instead of NCCL."""
+        if self.tp.size > 1 and self.tp.peers is None:
+            from .comm import PeerGroup
+            dev = self.rope_cos.device
+            self.tp.peers = PeerGroup(self.tp.size, self.tp.rank, dev, max_rows, self.cfg.hidden_size,
+                                      group=self.tp.group)
 
     @staticmethod
     def _attend(q16: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, T: int, rows: int) -> torch.Tensor:
