@@ -65,6 +65,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const T* __restrict__ q, 
                                                        const long long* __restrict__ pos, __half* __restrict__ kc,
                                                        __half* __restrict__ vc, int max_len, __half* __restrict__ qout)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     const int lane = threadIdx.x & 31;
     const int heads = hq + 2 * hkv;
     const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -108,6 +110,8 @@ __global__ void __launch_bounds__(256) add_norm_rot_kernel(const T* __restrict__
                                                            T* __restrict__ x_out, T* __restrict__ xn,
                                                            __half* __restrict__ xh)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     __shared__ float part[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.y;
@@ -187,18 +191,18 @@ extern "C" int exl3_qkv_post(const void* q, const void* k, const void* v, int q_
     __half* qo = static_cast<__half*>(q_out);
     switch (dtype) {
     case EXL3_F16:
-        qkv_post_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(q), static_cast<const __half*>(k),
+        if (int e_ = launch_pdl(qkv_post_kernel<__half>, grid, 128, 0, s, static_cast<const __half*>(q), static_cast<const __half*>(k),
                                                      static_cast<const __half*>(v), q_stride, k_stride, v_stride,
                                                      rows, hq, hkv,
                                                      static_cast<const __half*>(q_norm_w),
                                                      static_cast<const __half*>(k_norm_w), eps, cos_table, sin_table,
-                                                     pos, kc, vc, max_len, qo);
+                                                     pos, kc, vc, max_len, qo)) return e_;
         break;
     case EXL3_BF16:
-        qkv_post_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+        if (int e_ = launch_pdl(qkv_post_kernel<__nv_bfloat16>, grid, 128, 0, s, 
             static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
             static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, rows, hq, hkv, static_cast<const __nv_bfloat16*>(q_norm_w),
-            static_cast<const __nv_bfloat16*>(k_norm_w), eps, cos_table, sin_table, pos, kc, vc, max_len, qo);
+            static_cast<const __nv_bfloat16*>(k_norm_w), eps, cos_table, sin_table, pos, kc, vc, max_len, qo)) return e_;
         break;
     default: return EXL3_E_DTYPE;
     }
@@ -218,15 +222,15 @@ extern "C" int exl3_add_norm_rot(const void* x, const void* d, const void* w, in
     __half* o = static_cast<__half*>(xh);
     switch (dtype) {
     case EXL3_F16:
-        add_norm_rot_kernel<__half><<<grid, 256, 0, s>>>(
+        if (int e_ = launch_pdl(add_norm_rot_kernel<__half>, grid, 256, 0, s, 
             static_cast<const __half*>(x), static_cast<const __half*>(d), static_cast<const __half*>(w), eps, sh,
-            n_members, rows, k, static_cast<__half*>(x_out), static_cast<__half*>(xn), o);
+            n_members, rows, k, static_cast<__half*>(x_out), static_cast<__half*>(xn), o)) return e_;
         break;
     case EXL3_BF16:
-        add_norm_rot_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        if (int e_ = launch_pdl(add_norm_rot_kernel<__nv_bfloat16>, grid, 256, 0, s, 
             static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(d),
             static_cast<const __nv_bfloat16*>(w), eps, sh, n_members, rows, k, static_cast<__nv_bfloat16*>(x_out),
-            static_cast<__nv_bfloat16*>(xn), o);
+            static_cast<__nv_bfloat16*>(xn), o)) return e_;
         break;
     default: return EXL3_E_DTYPE;
     }

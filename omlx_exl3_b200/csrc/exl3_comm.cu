@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(kArThreads) ar_add_norm_rot_kernel(const exl3_
                                                                      int kd, T* __restrict__ x_out,
                                                                      T* __restrict__ xn, __half* __restrict__ xh)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     __shared__ float hbuf[kArChunk];                     // the chunk after add, then after norm
     __shared__ float part[kArThreads / 32];
     __shared__ uint32_t s_epoch;
@@ -296,14 +298,14 @@ extern "C" int exl3_ar_add_norm_rot(const exl3_peer_group* g, int slot, const vo
     __half* o = static_cast<__half*>(xh);
     switch (dtype) {
     case EXL3_F16:
-        ar_add_norm_rot_kernel<__half><<<grid, kArThreads, 0, s>>>(
+        if (int e_ = launch_pdl(ar_add_norm_rot_kernel<__half>, grid, kArThreads, 0, s, 
             *g, slot, static_cast<const __half*>(x), static_cast<const __half*>(w), eps, sh, n_members, rows, k,
-            static_cast<__half*>(x_out), static_cast<__half*>(xn), o);
+            static_cast<__half*>(x_out), static_cast<__half*>(xn), o)) return e_;
         break;
     case EXL3_BF16:
-        ar_add_norm_rot_kernel<__nv_bfloat16><<<grid, kArThreads, 0, s>>>(
+        if (int e_ = launch_pdl(ar_add_norm_rot_kernel<__nv_bfloat16>, grid, kArThreads, 0, s, 
             *g, slot, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), eps, sh,
-            n_members, rows, k, static_cast<__nv_bfloat16*>(x_out), static_cast<__nv_bfloat16*>(xn), o);
+            n_members, rows, k, static_cast<__nv_bfloat16*>(x_out), static_cast<__nv_bfloat16*>(xn), o)) return e_;
         break;
     default: return EXL3_E_DTYPE;
     }

@@ -171,6 +171,11 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
     };
 #pragma unroll 1
     for (int d = 0; d < S::DEPTH - 1; ++d) fetch();
+    // The weights are constant; everything from here on (xh, y, the split-k scratch) may be written or
+    // read by the previous kernel in the stream, so under programmatic dependent launch the ring fill
+    // above overlaps that kernel and the rest waits for it.
+    pdl_trigger();
+    pdl_wait();
     int cslot = 0;                                            // ring slot of the unit being decoded
 
     const int g = lane >> 2, q = lane & 3;
@@ -439,7 +444,7 @@ static int launch_gemv_v(const GemvParams& prm, int grid, cudaStream_t s)
             return EXL3_E_CUDA;
         attr_set[dev] = true;
     }
-    gemv_kernel<K, CB, kNCW, ROWS1><<<grid, S::THREADS, S::SMEM, s>>>(prm);
+    if (int e_ = launch_pdl(gemv_kernel<K, CB, kNCW, ROWS1>, grid, S::THREADS, S::SMEM, s, prm)) return e_;
     return launch_status();
 }
 

@@ -53,6 +53,8 @@ template <typename T>
 __global__ void __launch_bounds__(128) rot_kernel(const T* __restrict__ x, const __half* __restrict__ suh, int nm,
                                                   int rows, int kd, __half* __restrict__ xh)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * 4 + (threadIdx.x >> 5);   // (row, block)
     const int nblk = kd / 128;
@@ -71,6 +73,8 @@ __global__ void __launch_bounds__(256) norm_rot_kernel(const T* __restrict__ x, 
                                                        const __half* __restrict__ suh, int nm, int rows, int kd,
                                                        T* __restrict__ xn, __half* __restrict__ xh)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     __shared__ float part[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.y;
@@ -109,6 +113,8 @@ template <typename T>
 __global__ void __launch_bounds__(128) swiglu_rot_kernel(const T* __restrict__ gu, const __half* __restrict__ suh,
                                                          int rows, int n, __half* __restrict__ xh)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
     const int nblk = n / 128;
@@ -133,6 +139,8 @@ template <typename T, typename OT>
 __global__ void __launch_bounds__(128) had_svh_kernel(const T* __restrict__ y, const __half* __restrict__ svh,
                                                       int rows, int n, OT* __restrict__ out)
 {
+    pdl_trigger();                                   // the next kernel may start launching
+    pdl_wait();                                      // inputs written by the previous kernel
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
     const int nblk = n / 128;
@@ -155,11 +163,11 @@ static int launch_had_svh(const void* y, int rows, int n, const __half* svh, voi
 {
     const T* yy = static_cast<const T*>(y);
     switch (out_dtype) {
-    case EXL3_F16: had_svh_kernel<T, __half><<<grid, 128, 0, s>>>(yy, svh, rows, n, static_cast<__half*>(out)); break;
+    case EXL3_F16: if (int e_ = launch_pdl(had_svh_kernel<T, __half>, grid, 128, 0, s, yy, svh, rows, n, static_cast<__half*>(out))) return e_; break;
     case EXL3_BF16:
-        had_svh_kernel<T, __nv_bfloat16><<<grid, 128, 0, s>>>(yy, svh, rows, n, static_cast<__nv_bfloat16*>(out));
+        if (int e_ = launch_pdl(had_svh_kernel<T, __nv_bfloat16>, grid, 128, 0, s, yy, svh, rows, n, static_cast<__nv_bfloat16*>(out))) return e_;
         break;
-    case EXL3_F32: had_svh_kernel<T, float><<<grid, 128, 0, s>>>(yy, svh, rows, n, static_cast<float*>(out)); break;
+    case EXL3_F32: if (int e_ = launch_pdl(had_svh_kernel<T, float>, grid, 128, 0, s, yy, svh, rows, n, static_cast<float*>(out))) return e_; break;
     default: return EXL3_E_DTYPE;
     }
     return launch_status();
@@ -198,11 +206,11 @@ extern "C" int exl3_rot(const void* x, int x_dtype, int rows, int k, const void*
     const __half* sh = static_cast<const __half*>(suh);
     __half* o = static_cast<__half*>(xh);
     switch (x_dtype) {
-    case EXL3_F16: rot_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(x), sh, n_members, rows, k, o); break;
+    case EXL3_F16: if (int e_ = launch_pdl(rot_kernel<__half>, grid, 128, 0, s, static_cast<const __half*>(x), sh, n_members, rows, k, o)) return e_; break;
     case EXL3_BF16:
-        rot_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(x), sh, n_members, rows, k, o);
+        if (int e_ = launch_pdl(rot_kernel<__nv_bfloat16>, grid, 128, 0, s, static_cast<const __nv_bfloat16*>(x), sh, n_members, rows, k, o)) return e_;
         break;
-    case EXL3_F32: rot_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(x), sh, n_members, rows, k, o); break;
+    case EXL3_F32: if (int e_ = launch_pdl(rot_kernel<float>, grid, 128, 0, s, static_cast<const float*>(x), sh, n_members, rows, k, o)) return e_; break;
     default: return EXL3_E_DTYPE;
     }
     return launch_status();
@@ -220,13 +228,13 @@ extern "C" int exl3_norm_rot(const void* x, const void* w, int dtype, int rows, 
     __half* o = static_cast<__half*>(xh);
     switch (dtype) {
     case EXL3_F16:
-        norm_rot_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(w), eps,
-                                                     sh, n_members, rows, k, static_cast<__half*>(xn), o);
+        if (int e_ = launch_pdl(norm_rot_kernel<__half>, grid, 256, 0, s, static_cast<const __half*>(x), static_cast<const __half*>(w), eps,
+                                                     sh, n_members, rows, k, static_cast<__half*>(xn), o)) return e_;
         break;
     case EXL3_BF16:
-        norm_rot_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        if (int e_ = launch_pdl(norm_rot_kernel<__nv_bfloat16>, grid, 256, 0, s, 
             static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), eps, sh, n_members, rows, k,
-            static_cast<__nv_bfloat16*>(xn), o);
+            static_cast<__nv_bfloat16*>(xn), o)) return e_;
         break;
     default: return EXL3_E_DTYPE;
     }
@@ -244,11 +252,11 @@ extern "C" int exl3_swiglu_rot(const void* gu, int gu_dtype, int rows, int n, co
     const __half* sh = static_cast<const __half*>(suh);
     __half* o = static_cast<__half*>(xh);
     switch (gu_dtype) {
-    case EXL3_F16: swiglu_rot_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(gu), sh, rows, n, o); break;
+    case EXL3_F16: if (int e_ = launch_pdl(swiglu_rot_kernel<__half>, grid, 128, 0, s, static_cast<const __half*>(gu), sh, rows, n, o)) return e_; break;
     case EXL3_BF16:
-        swiglu_rot_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(gu), sh, rows, n, o);
+        if (int e_ = launch_pdl(swiglu_rot_kernel<__nv_bfloat16>, grid, 128, 0, s, static_cast<const __nv_bfloat16*>(gu), sh, rows, n, o)) return e_;
         break;
-    case EXL3_F32: swiglu_rot_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(gu), sh, rows, n, o); break;
+    case EXL3_F32: if (int e_ = launch_pdl(swiglu_rot_kernel<float>, grid, 128, 0, s, static_cast<const float*>(gu), sh, rows, n, o)) return e_; break;
     default: return EXL3_E_DTYPE;
     }
     return launch_status();
