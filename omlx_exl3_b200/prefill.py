@@ -12,10 +12,10 @@ import torch
 from .kernels import decode_wt, gemm, had_svh, rot
 
 PREFILL_COL_CHUNK = 16384
-# Up to this many rows the fused kernel is the faster of the two (measured on B200 at the 27B-class
-# shapes: it decodes every weight once per 256 rows, which costs more than one fp16 round trip of W
-# through HBM once the row count is large).
-FUSED_MAX_ROWS = 1024
+# Up to this many rows (one 256-row tile: every weight decoded once) the fused kernel is used. Above
+# it the fused kernel decodes every weight once per 256 rows, and on B200 at the 27B-class shapes
+# decoding W once to fp16 plus a library GEMM is already as fast at 512 rows and faster beyond.
+FUSED_MAX_ROWS = 256
 
 
 def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, cb: int, suh: torch.Tensor,
