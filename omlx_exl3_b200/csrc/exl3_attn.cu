@@ -117,11 +117,7 @@ __global__ void __launch_bounds__(256) add_norm_rot_kernel(const T* __restrict__
     const int r = blockIdx.y;
     const T* xr = x + (size_t)r * kd;
     const T* dr = d + (size_t)r * kd;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < kd; i += 256) {
-        const float a = to_f32(from_f32<T>(to_f32(xr[i]) + to_f32(dr[i])));
-        ss = fmaf(a, a, ss);
-    }
+    float ss = row_sumsq<T>(xr, dr, kd, threadIdx.x, 256);
     ss = warp_sum(ss);
     if (lane == 0) part[warp] = ss;
     __syncthreads();

@@ -363,4 +363,37 @@ constexpr float kHadScale = 0.08838834764831845f;   // 1/sqrt(128)
 // Error bits written to a caller-visible status word when a bounded wait gives up.
 enum : uint32_t { kStatusPipeTimeout = 1u, kStatusArrivalTimeout = 2u };
 
+// ------------------------------------------------------------------------------ row sums of squares
+// Sum over the row of T(x + d)^2 (d may be null: T(x)^2), fp32, this thread's share; 16-byte loads,
+// several in flight, when both rows are 16-byte aligned (the usual case), else element by element.
+template <typename T>
+__device__ __forceinline__ float row_sumsq(const T* __restrict__ xr, const T* __restrict__ dr, int kd, int tid,
+                                           int nthr)
+{
+    float ss = 0.f;
+    const bool vec = ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(dr)) & 15) == 0 && kd % 8 == 0;
+    if (vec) {
+        const uint4* x4 = reinterpret_cast<const uint4*>(xr);
+        const uint4* d4 = reinterpret_cast<const uint4*>(dr);
+#pragma unroll 4
+        for (int v = tid; v < kd / 8; v += nthr) {
+            const uint4 a = x4[v];
+            const uint4 b = dr ? d4[v] : make_uint4(0, 0, 0, 0);
+            const T* ae = reinterpret_cast<const T*>(&a);
+            const T* be = reinterpret_cast<const T*>(&b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float h = dr ? to_f32(from_f32<T>(to_f32(ae[i]) + to_f32(be[i]))) : to_f32(ae[i]);
+                ss = fmaf(h, h, ss);
+            }
+        }
+    } else {
+        for (int i = tid; i < kd; i += nthr) {
+            const float h = dr ? to_f32(from_f32<T>(to_f32(xr[i]) + to_f32(dr[i]))) : to_f32(xr[i]);
+            ss = fmaf(h, h, ss);
+        }
+    }
+    return ss;
+}
+
 }  // namespace exl3

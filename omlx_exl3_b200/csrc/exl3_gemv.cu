@@ -326,11 +326,20 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             if (finish) {
                 const int c_first = owner_cta((long long)b * KT / gran, U, G);
                 const int c_last = owner_cta(((long long)(b + 1) * KT - 1) / gran, U, G);
+                // CTA c_first holds the block in its slot jj0, every later CTA in its slot 0. The loads
+                // go out in batches of 8 before any add (an add per load would serialise the L2
+                // round trips); the adds stay in CTA order.
+                const int jj0 = b - (int)(cta_start(c_first, U, G) * gran / KT);
                 for (int e = ctid; e < rows * 128; e += 32 * NCW) {
-                    float v = 0.f;
-                    for (int cc = c_first; cc <= c_last; ++cc) {
-                        const int jj = cc == c_first ? b - (int)(cta_start(cc, U, G) * gran / KT) : 0;
-                        v += __ldcg(p.partials + ((size_t)cc * p.J + jj) * kRedStride + e);
+                    float v = __ldcg(p.partials + ((size_t)c_first * p.J + jj0) * kRedStride + e);
+                    for (int cc = c_first + 1; cc <= c_last; cc += 8) {
+                        float t[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            t[i] = cc + i <= c_last ? __ldcg(p.partials + (size_t)(cc + i) * p.J * kRedStride + e) : 0.f;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            if (cc + i <= c_last) v += t[i];
                     }
                     red[e] = v;
                 }
@@ -369,7 +378,9 @@ struct GemvLaunch {
 // (the CTA-wide reduction; more when the block is split over CTAs: publish, fence, arrival ticket,
 // the last arriver's sum). Measured on B200 at the 27B-class shapes, one segment end costs about
 // as much as decoding 15 units, a split one about 45. Candidates: one CTA per SM, and grids that
-// split every block evenly (s CTAs per block) or give every CTA d whole blocks.
+// split every block evenly (s CTAs per block) or give every CTA d whole blocks. (Splitting a block
+// over a thread-block cluster and summing in distributed shared memory was measured too: a few
+// percent faster on some shapes, slower overall, since clusters must be co-scheduled in one GPC.)
 static long long grid_cost(int blocks, int KT, int gran, long long G)
 {
     constexpr long long kWholeEnd = 15, kSplitEnd = 45;

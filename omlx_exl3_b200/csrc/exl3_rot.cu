@@ -79,11 +79,7 @@ __global__ void __launch_bounds__(256) norm_rot_kernel(const T* __restrict__ x, 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.y;
     const T* xr = x + (size_t)r * kd;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < kd; i += 256) {
-        const float a = to_f32(xr[i]);
-        ss = fmaf(a, a, ss);
-    }
+    float ss = row_sumsq<T>(xr, nullptr, kd, threadIdx.x, 256);
 #pragma unroll
     for (int h = 16; h >= 1; h >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, h);
     if (lane == 0) part[warp] = ss;
