@@ -25,7 +25,9 @@
 // * 1/sqrt(128) * svh, and writes y in the output dtype. No CTA ever waits on another CTA.
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "exl3_b200.h"
 #include "exl3_common.cuh"
@@ -65,14 +67,15 @@ struct GemvShape {
     static constexpr int THREADS = 32 * NCW;
 };
 
-__device__ __forceinline__ int owner_cta(long long u, long long U, int G)
+// 32-bit: the host guarantees units * (grid + 1) < 2^32
+__device__ __forceinline__ int owner_cta(unsigned u, unsigned U, unsigned G)
 {
-    return (int)(((u + 1) * (long long)G - 1) / U);
+    return (int)(((u + 1) * G - 1) / U);
 }
 
-__device__ __forceinline__ long long cta_start(int c, long long U, int G)
+__device__ __forceinline__ int cta_start(unsigned c, unsigned U, unsigned G)
 {
-    return (long long)c * U / G;
+    return (int)(c * U / G);
 }
 
 // 128-point FWHT of one row held by one warp as v[i] = column lane + 32 i, then scale, svh, store.
@@ -121,8 +124,8 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
     // CTA ranges are whole granules of p.gran units (16 when k is a multiple of 256), so every block
     // segment inside a CTA is a whole number of rounds of the NCW warps
     const int gran = p.gran;
-    const long long U = p.units / gran;
-    const long long u0 = cta_start(c, U, G) * gran, u1 = cta_start(c + 1, U, G) * gran;
+    const unsigned U = (unsigned)(p.units / gran);
+    const int u0 = cta_start(c, U, G) * gran, u1 = cta_start(c + 1, U, G) * gran;
     const int n_units = (int)(u1 - u0);
     const int KT = p.KT;
     const int rows = p.rows;
@@ -140,9 +143,9 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
     const uint32_t* fsrc = nullptr;
     size_t fstep = 0;                                                 // words between k-slices NCW apart
     auto fseek = [&]() {
-        const long long u = u0 + fi;
+        const int u = u0 + fi;
         fb = (int)(u / KT);
-        fkt = (int)(u - (long long)fb * KT);
+        fkt = u - fb * KT;
         const int m = (p.nm > 1 && fb >= p.blk_off[1]) ? ((p.nm > 2 && fb >= p.blk_off[2]) ? 2 : 1) : 0;
         const int ntm = m == 0 ? p.nt_member[0] : (m == 1 ? p.nt_member[1] : p.nt_member[2]);
         const int off = m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]);
@@ -186,8 +189,8 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
     for (int b = b_first; b <= b_last; ++b) {
         const int m = (p.nm > 1 && b >= p.blk_off[1]) ? ((p.nm > 2 && b >= p.blk_off[2]) ? 2 : 1) : 0;
         const __half* xrow = p.xh + ((size_t)m * rows + (ROWS1 ? 0 : g)) * p.k;
-        const int sa = (int)(max(u0, (long long)b * KT) - u0);
-        const int se = (int)(min(u1, (long long)(b + 1) * KT) - u0);
+        const int sa = max(u0, b * KT) - u0;
+        const int se = min(u1, (b + 1) * KT) - u0;
 
         // MMA path: acc[j] = the m16n8 accumulator of tile j. rows == 1 path: acc[j][0] / [1] are
         // columns g / g+8 of tile j in fp32, fed from half2 accumulators hacc every kFlush units.
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
         }
         int since_flush = 0;
 
-        const int kt_base = (int)(u0 - (long long)b * KT);     // k-slice of unit index 0 (may be < 0)
+        const int kt_base = u0 - b * KT;                     // k-slice of unit index 0 (may be < 0)
         int i = sa + ((cw - sa) % NCW + NCW) % NCW;
         // the lane's xh values for the next unit are fetched one unit ahead
         const __half* xp = xrow + (kt_base + i) * 16 + 2 * q;
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
         }
         __syncthreads();
 
-        const bool whole = (long long)b * KT >= u0 && (long long)(b + 1) * KT <= u1;
+        const bool whole = b * KT >= u0 && (b + 1) * KT <= u1;
         bool finish = whole;
         if (!whole) {
             // one warp publishes the CTA's partial and takes the block's arrival ticket
@@ -313,8 +316,8 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
                 __threadfence();
                 __syncwarp();
                 if (lane == 0) {
-                    const int c_first = owner_cta((long long)b * KT / gran, U, G);
-                    const int c_last = owner_cta(((long long)(b + 1) * KT - 1) / gran, U, G);
+                    const int c_first = owner_cta(b * KT / gran, U, G);
+                    const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
                     const unsigned old = atomicAdd(&p.counters[b], 1u);
                     const int last = old == (unsigned)(c_last - c_first);
                     if (last) __threadfence();
@@ -324,8 +327,8 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             __syncthreads();
             finish = s_last != 0;
             if (finish) {
-                const int c_first = owner_cta((long long)b * KT / gran, U, G);
-                const int c_last = owner_cta(((long long)(b + 1) * KT - 1) / gran, U, G);
+                const int c_first = owner_cta(b * KT / gran, U, G);
+                const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
                 // CTA c_first holds the block in its slot jj0, every later CTA in its slot 0. The loads
                 // go out in batches of 8 before any add (an add per load would serialise the L2
                 // round trips); the adds stay in CTA order.
@@ -399,7 +402,7 @@ static long long grid_cost(int blocks, int KT, int gran, long long G)
     return worst;
 }
 
-static int pick_grid(int blocks, int KT, int gran, int sms)
+static int pick_grid_uncached(int blocks, int KT, int gran, int sms)
 {
     long long best_g = sms, best = grid_cost(blocks, KT, gran, sms);
     auto consider = [&](long long g) {
@@ -408,12 +411,29 @@ static int pick_grid(int blocks, int KT, int gran, int sms)
         if (c < best) { best = c; best_g = g; }
     };
     if (blocks <= sms) {
-        for (int sp = sms / blocks; sp >= 1 && sp * blocks * 2 > sms; --sp) consider((long long)sp * blocks);
+        for (int sp = sms / blocks; sp >= 1; --sp) consider((long long)sp * blocks);
     } else {
         for (int dd = 2; dd <= 8; ++dd)
             if (blocks % dd == 0) consider(blocks / dd);
     }
     return (int)best_g;
+}
+
+// The choice is cached per (blocks, KT, gran, SMs): exl3_gemv plans on every call.
+static int pick_grid(int blocks, int KT, int gran, int sms)
+{
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, int>, int> cache;
+    const auto key = std::make_tuple(blocks, KT, gran, sms);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    const int g = pick_grid_uncached(blocks, KT, gran, sms);
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = g;
+    return g;
 }
 
 static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
@@ -437,6 +457,7 @@ static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
     long long G = d->grid > 0 ? d->grid : pick_grid(blocks, L->KT, L->gran, device_sm_count());
     if (G > granules) G = granules;
     L->grid = (int)G;
+    if ((unsigned long long)L->units * (unsigned long long)(G + 1) >= (1ull << 32)) return EXL3_E_SHAPE;
     const long long per = (granules + G - 1) / G * L->gran;
     L->J = (int)((per + L->KT - 1) / L->KT + 1);
     return EXL3_OK;
