@@ -68,6 +68,13 @@ struct GemvShape {
 };
 
 // 32-bit: the host guarantees units * (grid + 1) < 2^32
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(uint32_t* p, unsigned v)
+{
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ int owner_cta(unsigned u, unsigned U, unsigned G)
 {
     return (int)(((u + 1) * G - 1) / U);
@@ -313,15 +320,14 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             if (cw == 0) {
                 float* gp = p.partials + ((size_t)c * p.J + (b - b_first)) * kRedStride;
                 for (int e = lane; e < rows * 128; e += 32) gp[e] = red[e];
-                __threadfence();
-                __syncwarp();
+                __syncwarp();                                // the warp's stores, ordered before lane 0's release
                 if (lane == 0) {
                     const int c_first = owner_cta(b * KT / gran, U, G);
                     const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
-                    const unsigned old = atomicAdd(&p.counters[b], 1u);
-                    const int last = old == (unsigned)(c_last - c_first);
-                    if (last) __threadfence();
-                    s_last = last;
+                    // one acquire-release RMW: publishes this CTA's partial and, for the last arriver,
+                    // makes every other CTA's partial visible (no separate fences)
+                    const unsigned old = atom_add_acq_rel_gpu(&p.counters[b], 1u);
+                    s_last = old == (unsigned)(c_last - c_first);
                 }
             }
             __syncthreads();
