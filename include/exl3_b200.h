@@ -170,10 +170,36 @@ EXL3_API int exl3_qkv_post(const void* q, const void* k, const void* v, int q_st
                            void* v_cache, int max_len, void* q_out, void* stream);
 
 /*
+ * The q/k/v sibling group's GEMV with exl3_qkv_post as its epilogue: members 0/1/2 are q (hq heads),
+ * k and v (hkv heads each, head_dim 128). Each finished 128-column block is one head; it is rounded to
+ * desc->out_dtype exactly as exl3_gemv would store it and then written as exl3_qkv_post writes it
+ * (q_out fp16 (rows, hq, 128); k/v into the fp16 caches at pos[r]). No y. Same scratch as exl3_gemv.
+ * Replaces: kernels.TrellisGemvPlan for the q/k/v group + the attention module's q/k norm, RoPE and
+ * cache update (see exl3_qkv_post).
+ */
+typedef struct exl3_qkv_post_args {
+    const void* q_norm_w;        /* (128) in desc->out_dtype */
+    const void* k_norm_w;
+    const float* cos_table;      /* (max positions, 64) */
+    const float* sin_table;
+    const long long* pos;        /* (rows) int64 */
+    void* k_cache;               /* fp16 (hkv, max_len, 128) */
+    void* v_cache;
+    void* q_out;                 /* fp16 (rows, hq, 128) */
+    int32_t hq, hkv, max_len;
+    float eps;
+} exl3_qkv_post_args;
+
+EXL3_API int exl3_gemv_qkv_post(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
+                                const void* svh, float* partials, uint32_t* counters, const exl3_qkv_post_args* post,
+                                void* stream);
+
+/*
  * Residual add fused into norm_rot: x_out = T(x + d); xn = T(w * T(x_out * rsqrt(mean(x_out^2) + eps)));
  * xh[m] = fp16(had128(xn * suh[m]) / sqrt(128)). Replaces: `h = x + attn_out` followed by
  * kernels.norm_rot (src/omlx/exl3/kernels.py:408-425, :461-473). x_out must not alias x or d
- * (every block of a row reads the whole row); k % 128 == 0; suh fp16 (n_members, k).
+ * (every block of a row reads the whole row); k % 128 == 0; suh fp16 (n_members, k); xn may be NULL
+ * (the norm output is then not stored).
  */
 EXL3_API int exl3_add_norm_rot(const void* x, const void* d, const void* w, int dtype, int rows, int k, float eps,
                                const void* suh, int n_members, void* x_out, void* xn, void* xh, void* stream);

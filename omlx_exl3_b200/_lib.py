@@ -47,6 +47,14 @@ class PeerGroupDesc(ctypes.Structure):
 PEER_HANDLE_BYTES = 64
 
 
+class QkvPostArgs(ctypes.Structure):
+    """exl3_qkv_post_args: the q/k/v GEMV epilogue's extra operands."""
+    _fields_ = [("q_norm_w", ctypes.c_void_p), ("k_norm_w", ctypes.c_void_p), ("cos_table", ctypes.c_void_p),
+                ("sin_table", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("k_cache", ctypes.c_void_p),
+                ("v_cache", ctypes.c_void_p), ("q_out", ctypes.c_void_p), ("hq", ctypes.c_int32),
+                ("hkv", ctypes.c_int32), ("max_len", ctypes.c_int32), ("eps", ctypes.c_float)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -60,6 +68,7 @@ SIGNATURES = {
     "exl3_gemv_reset": (_I, [_P, _SZ, _P]),
     "exl3_gemv": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P, _P, _P]),
     "exl3_gemv_noalloc": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P]),
+    "exl3_gemv_qkv_post": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P, ctypes.POINTER(QkvPostArgs), _P]),
     "exl3_rot": (_I, [_P, _I, _I, _I, _P, _I, _P, _P]),
     "exl3_norm_rot": (_I, [_P, _P, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
     "exl3_swiglu_rot": (_I, [_P, _I, _I, _I, _P, _P, _P]),

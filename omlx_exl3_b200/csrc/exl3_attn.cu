@@ -18,44 +18,6 @@
 
 namespace exl3 {
 
-__device__ __forceinline__ float warp_sum(float v)
-{
-#pragma unroll
-    for (int h = 16; h >= 1; h >>= 1) v += __shfl_xor_sync(0xffffffffu, v, h);
-    return v;
-}
-
-// x (4 values of a 128-vector in this lane) -> MLX-rounded RMSNorm with weight w
-template <typename T>
-__device__ __forceinline__ void head_rms(float (&v)[4], const T* __restrict__ w, float eps, int lane)
-{
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const T t = from_f32<T>(v[i] * inv);
-        v[i] = to_f32(from_f32<T>(to_f32(w[lane + 32 * i]) * to_f32(t)));
-    }
-}
-
-__device__ __forceinline__ void rope_half(float (&v)[4], const float* __restrict__ cs, const float* __restrict__ sn,
-                                          int lane)
-{
-    // elements c = lane + 32 i; pairs (c, c + 64) for c < 64: (v[0], v[2]) and (v[1], v[3]).
-    // Products and sums rounded separately (no contraction), as an elementwise framework op computes them.
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int c = lane + 32 * i;
-        const float x1 = v[i], x2 = v[i + 2];
-        const float co = cs[c], si = sn[c];
-        v[i] = __fsub_rn(__fmul_rn(x1, co), __fmul_rn(x2, si));
-        v[i + 2] = __fadd_rn(__fmul_rn(x2, co), __fmul_rn(x1, si));
-    }
-}
-
 template <typename T>
 __global__ void __launch_bounds__(128) qkv_post_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                        const T* __restrict__ v_in, int sq, int sk, int sv,
@@ -102,7 +64,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const T* __restrict__ q, 
 
 // One CTA per (row, group of 8 column blocks), as norm_rot. Every CTA of a row reads the whole row
 // of x and d for the sum of squares, so the new residual goes to a separate buffer x_out (x_out must
-// not alias x or d).
+// not alias x or d). A warp issues every load of its own block (x, d, w, each member's suh) before
+// the row reduction, so their latency overlaps it. xn may be null (not stored).
 template <typename T>
 __global__ void __launch_bounds__(256) add_norm_rot_kernel(const T* __restrict__ x, const T* __restrict__ d,
                                                            const T* __restrict__ w, float eps,
@@ -117,33 +80,50 @@ __global__ void __launch_bounds__(256) add_norm_rot_kernel(const T* __restrict__
     const int r = blockIdx.y;
     const T* xr = x + (size_t)r * kd;
     const T* dr = d + (size_t)r * kd;
+    const int blk = blockIdx.x * 8 + warp;
+    const bool active = blk < kd / 128;
+    const int c0 = blk * 128;
+    float xs[4], ds[4], ws[4], su[3][4];
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = c0 + lane + 32 * i;
+            xs[i] = to_f32(xr[c]);
+            ds[i] = to_f32(dr[c]);
+            ws[i] = to_f32(w[c]);
+        }
+#pragma unroll
+        for (int m = 0; m < 3; ++m)
+            if (m < nm)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) su[m][i] = __half2float(suh[(size_t)m * kd + c0 + lane + 32 * i]);
+    }
     float ss = row_sumsq<T>(xr, dr, kd, threadIdx.x, 256);
     ss = warp_sum(ss);
     if (lane == 0) part[warp] = ss;
     __syncthreads();
+    if (!active) return;
     float tot = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) tot += part[i];
     const float inv = 1.0f / sqrtf(tot / (float)kd + eps);
-
-    const int blk = blockIdx.x * 8 + warp;
-    if (blk >= kd / 128) return;
-    const int c0 = blk * 128;
     float xv[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int c = c0 + lane + 32 * i;
-        const T s = from_f32<T>(to_f32(xr[c]) + to_f32(dr[c]));
+        const T s = from_f32<T>(xs[i] + ds[i]);
         const T t = from_f32<T>(to_f32(s) * inv);
-        const T o = from_f32<T>(to_f32(w[c]) * to_f32(t));
+        const T o = from_f32<T>(ws[i] * to_f32(t));
         x_out[(size_t)r * kd + c] = s;
-        xn[(size_t)r * kd + c] = o;
+        if (xn) xn[(size_t)r * kd + c] = o;
         xv[i] = to_f32(o);
     }
-    for (int m = 0; m < nm; ++m) {
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        if (m >= nm) break;
         float v[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = xv[i] * __half2float(suh[(size_t)m * kd + c0 + lane + 32 * i]);
+        for (int i = 0; i < 4; ++i) v[i] = xv[i] * su[m][i];
 #pragma unroll
         for (int h = 1; h < 32; h <<= 1) {
 #pragma unroll
@@ -208,7 +188,7 @@ extern "C" int exl3_qkv_post(const void* q, const void* k, const void* v, int q_
 extern "C" int exl3_add_norm_rot(const void* x, const void* d, const void* w, int dtype, int rows, int k, float eps,
                                  const void* suh, int n_members, void* x_out, void* xn, void* xh, void* stream)
 {
-    if (!x || !d || !w || !suh || !x_out || !xn || !xh) return EXL3_E_NULL;
+    if (!x || !d || !w || !suh || !x_out || !xh) return EXL3_E_NULL;   // xn may be null
     if (rows < 1 || k <= 0 || k % 128 || n_members < 1 || n_members > 3) return EXL3_E_SHAPE;
     if (x_out == x || x_out == d) return EXL3_E_SHAPE;
     if (int e = check_device()) return e;

@@ -396,4 +396,45 @@ __device__ __forceinline__ float row_sumsq(const T* __restrict__ xr, const T* __
     return ss;
 }
 
+// ------------------------------------------------------------------------------ per-head q/k post-processing
+// (shared by exl3_qkv_post and the q/k/v GEMV epilogue) one warp holds a 128-vector as
+// v[i] = element lane + 32 i.
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int h = 16; h >= 1; h >>= 1) v += __shfl_xor_sync(0xffffffffu, v, h);
+    return v;
+}
+
+// x (4 values of a 128-vector in this lane) -> MLX-rounded RMSNorm with weight w
+template <typename T>
+__device__ __forceinline__ void head_rms(float (&v)[4], const T* __restrict__ w, float eps, int lane)
+{
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const T t = from_f32<T>(v[i] * inv);
+        v[i] = to_f32(from_f32<T>(to_f32(w[lane + 32 * i]) * to_f32(t)));
+    }
+}
+
+__device__ __forceinline__ void rope_half(float (&v)[4], const float* __restrict__ cs, const float* __restrict__ sn,
+                                          int lane)
+{
+    // elements c = lane + 32 i; pairs (c, c + 64) for c < 64: (v[0], v[2]) and (v[1], v[3]).
+    // Products and sums rounded separately (no contraction), as an elementwise framework op computes them.
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int c = lane + 32 * i;
+        const float x1 = v[i], x2 = v[i + 2];
+        const float co = cs[c], si = sn[c];
+        v[i] = __fsub_rn(__fmul_rn(x1, co), __fmul_rn(x2, si));
+        v[i + 2] = __fadd_rn(__fmul_rn(x2, co), __fmul_rn(x1, si));
+    }
+}
+
 }  // namespace exl3

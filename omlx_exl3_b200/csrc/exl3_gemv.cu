@@ -47,6 +47,8 @@ struct GemvParams {
     uint32_t* counters;      // blocks, then one status word
     int k, KT, rows, n_total, blocks, out_bf16, J, row_exact, gran;
     long long units;
+    int qkv;                 // 1: members are q, k, v and the finish is exl3_qkv_post's (no y)
+    exl3_qkv_post_args post;
 };
 
 constexpr int kRedStride = 8 * 128;   // floats per warp partial (8 rows x 128 columns)
@@ -86,8 +88,7 @@ __device__ __forceinline__ int cta_start(unsigned c, unsigned U, unsigned G)
 }
 
 // 128-point FWHT of one row held by one warp as v[i] = column lane + 32 i, then scale, svh, store.
-template <typename OT>
-__device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half* svh, OT* yrow)
+__device__ __forceinline__ void fwht128_rows(float (&v)[4], int lane)
 {
 #pragma unroll
     for (int h = 1; h < 32; h <<= 1) {
@@ -109,11 +110,50 @@ __device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half
         a0 = v[1]; a1 = v[3];
         v[1] = a0 + a1; v[3] = a0 - a1;
     }
+}
+
+template <typename OT>
+__device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half* svh, OT* yrow)
+{
+    fwht128_rows(v, lane);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int c = lane + 32 * i;
         yrow[c] = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
     }
+}
+
+// The q/k/v group's finish, fused with exl3_qkv_post: block b is one head of q (member 0), k (1) or
+// v (2). The GEMV value is rounded to the model dtype T exactly as a stored y would be, then q/k get
+// the per-head RMSNorm (MLX rounding) and rotate-half RoPE and go to q_out / the k cache, v to the v
+// cache, all at this row's position.
+template <typename T>
+__device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const __half* svh, const GemvParams& p, int b,
+                                           int r)
+{
+    fwht128_rows(v, lane);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = to_f32(from_f32<T>(v[i] * kHadScale * __half2float(svh[lane + 32 * i])));
+    const exl3_qkv_post_args& a = p.post;
+    const int m = b >= p.blk_off[2] ? 2 : (b >= p.blk_off[1] ? 1 : 0);
+    const int head = b - (m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]));
+    const long long pos = a.pos[r];
+    const float* cs = a.cos_table + (size_t)pos * 64;
+    const float* sn = a.sin_table + (size_t)pos * 64;
+    __half* o;
+    if (m == 0) {
+        head_rms<T>(v, static_cast<const T*>(a.q_norm_w), a.eps, lane);
+        rope_half(v, cs, sn, lane);
+        o = static_cast<__half*>(a.q_out) + ((size_t)r * a.hq + head) * 128;
+    } else if (m == 1) {
+        head_rms<T>(v, static_cast<const T*>(a.k_norm_w), a.eps, lane);
+        rope_half(v, cs, sn, lane);
+        o = static_cast<__half*>(a.k_cache) + ((size_t)head * a.max_len + pos) * 128;
+    } else {
+        o = static_cast<__half*>(a.v_cache) + ((size_t)head * a.max_len + pos) * 128;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[lane + 32 * i] = __float2half_rn(m == 2 ? v[i] : to_f32(from_f32<T>(v[i])));
 }
 
 template <int K, int CB, int NCW, bool ROWS1>
@@ -363,10 +403,14 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
                 for (int ii = 0; ii < 4; ++ii) v[ii] = red[r * 128 + lane + 32 * ii];
                 const __half* sv = p.svh + (size_t)b * 128;
                 const size_t yoff = (size_t)r * p.n_total + (size_t)b * 128;
-                if (p.out_bf16)
+                if (p.qkv) {
+                    if (p.out_bf16) finish_qkv<__nv_bfloat16>(v, lane, sv, p, b, r);
+                    else finish_qkv<__half>(v, lane, sv, p, b, r);
+                } else if (p.out_bf16) {
                     finish_row(v, lane, sv, reinterpret_cast<__nv_bfloat16*>(p.y) + yoff);
-                else
+                } else {
                     finish_row(v, lane, sv, reinterpret_cast<__half*>(p.y) + yoff);
+                }
             }
         }
         __syncthreads();   // red is reused by the next segment
@@ -523,13 +567,13 @@ extern "C" int exl3_gemv_reset(uint32_t* counters, size_t counter_bytes, void* s
                : EXL3_E_CUDA;
 }
 
-extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
-                         void* y, float* partials, uint32_t* counters, void* stream)
+static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
+                       void* y, float* partials, uint32_t* counters, const exl3_qkv_post_args* post, void* stream)
 {
     using namespace exl3;
     GemvLaunch L;
     if (int e = plan_gemv(desc, &L)) return e;
-    if (!xh || !trellis || !svh || !y || !partials || !counters) return EXL3_E_NULL;
+    if (!xh || !trellis || !svh || (!y && !post) || !partials || !counters) return EXL3_E_NULL;
     for (int m = 0; m < desc->n_members; ++m) {
         if (!trellis[m]) return EXL3_E_NULL;
         if (!aligned(trellis[m], 16)) return EXL3_E_ALIGN;
@@ -565,6 +609,8 @@ extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint3
     prm.row_exact = (desc->flags & EXL3_GEMV_ROW_EXACT) != 0;
     prm.units = L.units;
     prm.gran = L.gran;
+    prm.qkv = post != nullptr;
+    if (post) prm.post = *post;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (desc->bits) {
@@ -634,4 +680,24 @@ extern "C" int exl3_gemv_noalloc(const exl3_gemv_desc* desc, const void* xh, con
     if (cudaMemsetAsync(counters, 0, counter_bytes, static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return EXL3_E_CUDA;
     return exl3_gemv(desc, xh, trellis, svh, y, partials, counters, stream);
+}
+
+extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
+                         void* y, float* partials, uint32_t* counters, void* stream)
+{
+    return gemv_common(desc, xh, trellis, svh, y, partials, counters, nullptr, stream);
+}
+
+extern "C" int exl3_gemv_qkv_post(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
+                                  const void* svh, float* partials, uint32_t* counters,
+                                  const exl3_qkv_post_args* post, void* stream)
+{
+    if (!desc || !post) return EXL3_E_NULL;
+    if (!post->q_norm_w || !post->k_norm_w || !post->cos_table || !post->sin_table || !post->pos || !post->k_cache ||
+        !post->v_cache || !post->q_out)
+        return EXL3_E_NULL;
+    if (desc->n_members != 3 || post->hq < 1 || post->hkv < 1 || post->max_len < 1 || desc->n[0] != post->hq * 128 ||
+        desc->n[1] != post->hkv * 128 || desc->n[2] != post->hkv * 128)
+        return EXL3_E_SHAPE;
+    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, post, stream);
 }

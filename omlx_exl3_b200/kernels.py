@@ -101,6 +101,34 @@ class TrellisGemvPlan:
         return y
 
 
+    def qkv_post(self, xh: torch.Tensor, trellises: list[torch.Tensor], q_norm_w: torch.Tensor,
+                 k_norm_w: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
+                 k_cache: torch.Tensor, v_cache: torch.Tensor, q_out: torch.Tensor | None = None) -> torch.Tensor:
+        """For a q/k/v group plan: the GEMV with qkv_post as its epilogue (exl3_gemv_qkv_post). Writes this
+        step's k/v into the caches at pos and returns q (rows, hq, 128) fp16."""
+        assert self.nsub == 3 and len(trellises) == 3
+        hq, hkv = self.member_ns[0] // 128, self.member_ns[1] // 128
+        xh = xh.contiguous()
+        if xh.dtype != torch.float16 or xh.numel() != 3 * self.rows * self.k:
+            raise ValueError("xh must be fp16 (3, rows, k)")
+        _need_cuda(xh, *trellises)
+        assert k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape[0] == hkv
+        assert cos.dtype == sin.dtype == torch.float32 and pos.dtype == torch.int64
+        if q_out is None:
+            q_out = torch.empty((self.rows, hq, 128), dtype=torch.float16, device=xh.device)
+        a = _lib.QkvPostArgs()
+        a.q_norm_w, a.k_norm_w = q_norm_w.data_ptr(), k_norm_w.data_ptr()
+        a.cos_table, a.sin_table, a.pos = cos.data_ptr(), sin.data_ptr(), pos.data_ptr()
+        a.k_cache, a.v_cache, a.q_out = k_cache.data_ptr(), v_cache.data_ptr(), q_out.data_ptr()
+        a.hq, a.hkv, a.max_len, a.eps = hq, hkv, k_cache.shape[1], float(eps)
+        for i in range(3):
+            self._tptr[i] = trellises[i].data_ptr()
+        check(lib().exl3_gemv_qkv_post(ctypes.byref(self.desc), xh.data_ptr(), ctypes.cast(self._tptr, ctypes.c_void_p),
+                                       self.svh.data_ptr(), self.partials.data_ptr(), self.counters.data_ptr(),
+                                       ctypes.byref(a), stream_ptr(xh.device)), "exl3_gemv_qkv_post")
+        return q_out
+
+
 def decode_wt(trellis_u32: torch.Tensor, k: int, n: int, K: int, cb: int, nt0: int = 0, ntc: int | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """W_inner^T columns [16*nt0, 16*(nt0+ntc)) as an (16*ntc, k) fp16 matrix (rows = output features)."""
@@ -203,9 +231,10 @@ def qkv_post(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_w: torch.
     return q_out
 
 
-def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float,
-                 suh: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """h = x + d, RMSNorm(h) * w (MLX rounding) and its rotations: returns (h, xn, xh (NM, rows, K) fp16)."""
+def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float, suh: torch.Tensor,
+                 want_xn: bool = True) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
+    """h = x + d, RMSNorm(h) * w (MLX rounding) and its rotations: returns (h, xn, xh (NM, rows, K) fp16);
+    xn is None (not computed into memory) when want_xn is False."""
     rows, k = x.shape
     suh = suh.reshape(-1, k)
     nm = suh.shape[0]
@@ -215,11 +244,11 @@ def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float,
     w = w.to(x.dtype).contiguous()
     suh = suh.to(torch.float16).contiguous()
     h = torch.empty_like(x)
-    xn = torch.empty_like(x)
+    xn = torch.empty_like(x) if want_xn else None
     xh = torch.empty((nm, rows, k), dtype=torch.float16, device=x.device)
     check(lib().exl3_add_norm_rot(x.data_ptr(), d.data_ptr(), w.data_ptr(), dtype_code(x.dtype), rows, k, float(eps),
-                                  suh.data_ptr(), nm, h.data_ptr(), xn.data_ptr(), xh.data_ptr(),
-                                  stream_ptr(x.device)), "exl3_add_norm_rot")
+                                  suh.data_ptr(), nm, h.data_ptr(), xn.data_ptr() if xn is not None else None,
+                                  xh.data_ptr(), stream_ptr(x.device)), "exl3_add_norm_rot")
     return h, xn, xh
 
 

@@ -256,6 +256,10 @@ class _LayerDecode:
         # column slices of each projection inside the unit outputs: (unit index, column offset, width)
         self.qkv_at = [self._locate(self.qkv, lin) for lin in (a.q_proj, a.k_proj, a.v_proj)]
         self.gu_at = [self._locate(self.gate_up, lin) for lin in (m.gate_proj, m.up_proj)]
+        # one q/k/v sibling group in that order: its GEMV can finish with qkv_post as the epilogue
+        u = self.qkv.units[0]
+        self.qkv_group = (u if len(self.qkv.units) == 1 and not isinstance(u, EXL3Linear)
+                          and list(u.members) == [a.q_proj, a.k_proj, a.v_proj] else None)
 
     @staticmethod
     def _locate(t: _Targets, lin: EXL3Linear) -> tuple[int, int, int]:
@@ -314,8 +318,8 @@ class Qwen3EXL3(nn.Module):
         return self.lm_head(h) if self.lm_head is not None else h
 
     # -- fused decode step ----------------------------------------------------------------------
-    # rows <= MAX_GEMV_ROWS: per layer  [add+]norm+rotate -> q/k/v GEMV -> qkv_post (q/k norm, RoPE,
-    # cache write) -> attention -> rotate -> o GEMV -> all-reduce -> add+norm+rotate -> gate/up GEMV ->
+    # rows <= MAX_GEMV_ROWS: per layer  [add+]norm+rotate -> q/k/v GEMV with qkv_post (q/k norm, RoPE,
+    # cache write) as its epilogue -> attention -> rotate -> o GEMV -> all-reduce -> add+norm+rotate -> gate/up GEMV ->
     # SwiGLU+rotate -> down GEMV -> all-reduce; the MLP residual add is folded into the next layer's
     # input norm (and the last one into the final norm). Same arithmetic and roundings as the module
     # path above (the residual sums round to the model dtype in both).
@@ -365,7 +369,7 @@ class Qwen3EXL3(nn.Module):
 
         def add_norm(x, pend, w, suh):
             if peers is None:
-                return add_norm_rot(x, pend, w, eps, suh)
+                return add_norm_rot(x, pend, w, eps, suh, want_xn=False)
             return peers.ar_add_norm_rot(pend, x, w, eps, suh)
 
         for i, (layer, lp) in enumerate(zip(self.model.layers, self.__dict__["_decode_plans"])):
@@ -375,10 +379,15 @@ class Qwen3EXL3(nn.Module):
                 _, xh = norm_rot(x, w_in, eps, lp.qkv.suh)
             else:
                 x, _, xh = add_norm(x, pending, w_in, lp.qkv.suh)
-            outs = lp.qkv.outputs(xh, rows, dt)
             kc, vc = cache.k[i], cache.v[i]
-            q16 = qkv_post(_cols(outs, lp.qkv_at[0]), _cols(outs, lp.qkv_at[1]), _cols(outs, lp.qkv_at[2]),
-                           attn.q_norm.weight, attn.k_norm.weight, eps, self.rope_cos, self.rope_sin, pos, kc, vc)
+            if lp.qkv_group is not None:                    # q/k/v GEMV with qkv_post as its epilogue
+                g = lp.qkv_group
+                q16 = g.plan(rows, dt).qkv_post(xh, g.trs, attn.q_norm.weight, attn.k_norm.weight, eps,
+                                                self.rope_cos, self.rope_sin, pos, kc, vc)
+            else:
+                outs = lp.qkv.outputs(xh, rows, dt)
+                q16 = qkv_post(_cols(outs, lp.qkv_at[0]), _cols(outs, lp.qkv_at[1]), _cols(outs, lp.qkv_at[2]),
+                               attn.q_norm.weight, attn.k_norm.weight, eps, self.rope_cos, self.rope_sin, pos, kc, vc)
             o = self._attend(q16, kc, vc, T, rows)
             a = row_parallel(attn.o_proj, rot(o, attn.o_proj.rot_suh))
             x, _, xh = add_norm(x, a, layer.post_attention_layernorm.weight, lp.gate_up.suh)

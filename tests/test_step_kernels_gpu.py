@@ -109,3 +109,34 @@ def test_add_norm_rot_rejects_alias(cuda):
     rc = _lib.lib().exl3_add_norm_rot(x.data_ptr(), d.data_ptr(), w.data_ptr(), 1, 1, 1024, 1e-6, suh.data_ptr(), 1,
                                       x.data_ptr(), xn.data_ptr(), xh.data_ptr(), None)
     assert rc == -1     # EXL3_E_SHAPE
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,hq,hkv,K", [(1, 40, 8, 6), (3, 8, 2, 5), (8, 20, 4, 4)])
+def test_gemv_qkv_post_epilogue_matches_two_kernels(cuda, dtype, rows, hq, hkv, K):
+    """exl3_gemv_qkv_post == exl3_gemv (y in dtype) followed by exl3_qkv_post, bit for bit."""
+    from omlx_exl3_b200 import kernels
+    from omlx_exl3_b200.model import ModelConfig, rope_tables
+    k = 1024
+    ns = [hq * 128, hkv * 128, hkv * 128]
+    g = torch.Generator(device=cuda)
+    g.manual_seed(rows * 7 + hq + K)
+    trs = [torch.randint(-2 ** 31, 2 ** 31 - 1, (k * n * K // 32,), dtype=torch.int32, device=cuda, generator=g)
+           for n in ns]
+    svh = ((torch.randint(0, 2, (sum(ns),), device=cuda, generator=g) * 2 - 1) * 0.03).half()
+    xh = torch.randn((3, rows, k), device=cuda, generator=g).half()
+    qw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(dtype)
+    kw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(dtype)
+    cos, sin = rope_tables(ModelConfig(max_position_embeddings=700), cuda)
+    pos = torch.tensor([3, 650, 17, 0, 100, 101, 102, 400][:rows], dtype=torch.int64, device=cuda)
+    plan = kernels.TrellisGemvPlan(k, ns, K, 0, svh, rows, dtype)
+    kc1 = torch.zeros((hkv, 700, 128), dtype=torch.float16, device=cuda)
+    vc1, kc2, vc2 = torch.zeros_like(kc1), torch.zeros_like(kc1), torch.zeros_like(kc1)
+    y = plan(xh, trs)
+    q1 = kernels.qkv_post(y[:, :ns[0]], y[:, ns[0]:ns[0] + ns[1]], y[:, ns[0] + ns[1]:], qw, kw, 1e-6, cos, sin, pos,
+                          kc1, vc1)
+    q2 = plan.qkv_post(xh, trs, qw, kw, 1e-6, cos, sin, pos, kc2, vc2)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    assert plan.workspace_status() == 0
