@@ -218,26 +218,48 @@ EXL3_API int exl3_peer_open(const void* handle, void** ptr);
 EXL3_API int exl3_peer_close(void* ptr);
 
 /* One tensor-parallel group as seen by one rank. Buffer layout (byte offsets, same on every rank):
- * a 64-byte flag block at flag_off (zeroed at creation), and two partial slots of slot_bytes at
- * data_off and data_off + slot_bytes. */
+ * a flag block at flag_off (zeroed at creation; word 8 = epoch of the last completed all-reduce,
+ * word 9 = CTA arrival count, word 10 = status bits), then two slots, each holding `world` inboxes of
+ * inbox_bytes: the inbox of (slot s, source rank p) starts at data_off + (s * world + p) * inbox_bytes.
+ * An inbox holds one source rank's (rows, k) partial as "LL" words, 8 bytes per pair of columns:
+ * bits 0..31 the two 16-bit values (column 2j in the low half), bits 32..63 the epoch of the call
+ * that wrote them. A reader takes a word once its epoch matches, so data and flag arrive together. */
 typedef struct exl3_peer_group {
     int32_t world;           /* 1..8 */
     int32_t rank;            /* this process's rank */
     void* base[8];           /* every rank's buffer as mapped in this process (base[rank] = own) */
     uint64_t flag_off;       /* multiple of 64 */
     uint64_t data_off;       /* multiple of 16 */
-    uint64_t slot_bytes;     /* multiple of 16, >= rows * k * 2 */
+    uint64_t inbox_bytes;    /* multiple of 16, >= rows * k * 4 */
 } exl3_peer_group;
 
 /*
+ * Push this rank's (rows, k) partial (16-bit values, 4-byte aligned) into inbox (slot, rank) of every
+ * rank of the group, tagged with the epoch of the next exl3_ar_add_norm_rot. For producers other than
+ * exl3_gemv_peer. No counterpart in the reference (one Apple GPU).
+ */
+EXL3_API int exl3_peer_put(const exl3_peer_group* g, int slot, const void* src, int rows, int k, void* stream);
+
+/*
+ * exl3_gemv whose output rows go, as LL words, straight into inbox (slot, rank) of every rank of the
+ * group (P2P stores over NVLink from the CTAs that finish each 128-column block) instead of into y.
+ * The output width n_total is the all-reduce's k. Replaces: kernels.TrellisGemvPlan for a
+ * row-parallel projection followed by its all-reduce.
+ */
+EXL3_API int exl3_gemv_peer(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
+                            const void* svh, float* partials, uint32_t* counters, const exl3_peer_group* g, int slot,
+                            void* stream);
+
+/*
  * All-reduce of the row-parallel partials fused with residual add + RMSNorm + input rotation:
- *   d = sum over ranks (in rank order, fp32) of slot `slot` of every rank's buffer, (rows, k) of dtype T,
- *   then exactly exl3_add_norm_rot(x, T(d), w, ...). The caller's GEMV must have written this rank's
- *   partial into its own slot `slot`; consecutive calls alternate slot 0 / 1; every rank makes the
- *   same sequence of calls. Waits for the other ranks' flags at most 2 s, then sets a status bit
- *   (exl3_peer_status) and continues. Replaces: the NCCL all-reduce + exl3_add_norm_rot pair of the
- *   tensor-parallel decode step (the reference runs on one GPU; its norm-rotation is
- *   src/omlx/exl3/kernels.py:408-425). k % 128 == 0, k <= 16384, rows <= 8.
+ *   d = sum over ranks (in rank order, fp32) of the partials in this rank's inboxes of slot `slot`,
+ *   (rows, k) of dtype T, then exactly exl3_add_norm_rot(x, T(d), w, ...). Every rank must have
+ *   pushed its partial for this call (exl3_gemv_peer / exl3_peer_put) into slot `slot`; consecutive
+ *   calls alternate slot 0 / 1; every rank makes the same sequence of calls. Polls its own inboxes
+ *   for at most 2 s, then sets a status bit (exl3_peer_status) and continues. Replaces: the NCCL
+ *   all-reduce + exl3_add_norm_rot pair of the tensor-parallel decode step (the reference runs on
+ *   one GPU; its norm-rotation is src/omlx/exl3/kernels.py:408-425). k % 128 == 0, k <= 16384,
+ *   rows <= 8; x, w, suh, x_out 16-byte aligned; xn may be NULL.
  */
 EXL3_API int exl3_ar_add_norm_rot(const exl3_peer_group* g, int slot, const void* x, const void* w, int dtype,
                                   int rows, int k, float eps, const void* suh, int n_members, void* x_out,

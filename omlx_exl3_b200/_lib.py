@@ -41,7 +41,7 @@ GEMV_ROW_EXACT = 1
 class PeerGroupDesc(ctypes.Structure):
     """exl3_peer_group: one tensor-parallel group as seen by one rank."""
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("base", ctypes.c_void_p * 8),
-                ("flag_off", ctypes.c_uint64), ("data_off", ctypes.c_uint64), ("slot_bytes", ctypes.c_uint64)]
+                ("flag_off", ctypes.c_uint64), ("data_off", ctypes.c_uint64), ("inbox_bytes", ctypes.c_uint64)]
 
 
 PEER_HANDLE_BYTES = 64
@@ -83,6 +83,8 @@ SIGNATURES = {
     "exl3_ar_add_norm_rot": (_I, [ctypes.POINTER(PeerGroupDesc), _I, _P, _P, _I, _I, _I, _F, _P, _I, _P, _P, _P,
                                   _P]),
     "exl3_peer_status": (_I, [ctypes.POINTER(PeerGroupDesc), ctypes.POINTER(ctypes.c_uint32)]),
+    "exl3_peer_put": (_I, [ctypes.POINTER(PeerGroupDesc), _I, _P, _I, _I, _P]),
+    "exl3_gemv_peer": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P, ctypes.POINTER(PeerGroupDesc), _I, _P]),
 }
 
 

@@ -2,11 +2,12 @@
 
 One process per GPU. Each rank allocates one buffer (exl3_peer_create), the 64-byte CUDA IPC handles
 are exchanged with one all_gather over the group's process group, and every rank maps the others'
-buffers (exl3_peer_open). A row-parallel projection's GEMV writes its partial output straight into
-the rank's slot (slot_view); exl3_ar_add_norm_rot then sums all ranks' slots over NVLink and does
-the residual add, RMSNorm and input rotations of the next projection group in the same kernel. This
-replaces the NCCL all-reduce + add_norm_rot pair of the decode step (model.Qwen3EXL3); the
-reference has no tensor parallelism (one Apple GPU).
+buffers (exl3_peer_open). A row-parallel projection's GEMV pushes its partial output straight into
+every rank's inbox (kernels.TrellisGemvPlan.peer, or `put` for any other producer), as 8-byte words
+that carry the call's epoch next to the data; exl3_ar_add_norm_rot then waits on its own inboxes
+only, sums the ranks and does the residual add, RMSNorm and input rotations of the next projection
+group in the same kernel. This replaces the NCCL all-reduce + add_norm_rot pair of the decode step
+(model.Qwen3EXL3); the reference has no tensor parallelism (one Apple GPU).
 """
 from __future__ import annotations
 
@@ -32,12 +33,15 @@ class _DevArray:
 
 class PeerGroup:
     def __init__(self, world: int, rank: int, device: torch.device, max_rows: int, max_k: int, group=None,
-                 handles: list[bytes] | None = None):
-        """Collective over `group` unless `handles` (every rank's IPC handle, in rank order) is given."""
+                 handles: list[bytes] | None = None, capacity_world: int | None = None):
+        """Collective over `group` unless `handles` (every rank's IPC handle, in rank order) is given.
+        The buffer holds inboxes for `capacity_world` ranks (default `world`; tests that wire several
+        single-rank groups into one emulated group on one GPU size it for the emulated group)."""
         assert 1 <= world <= 8
         self.world, self.rank, self.device = world, rank, device
-        self.slot_bytes = ((max_rows * max_k * 2 + 255) // 256) * 256
-        self.nbytes = DATA_OFF + 2 * self.slot_bytes
+        self.max_rows, self.max_k = max_rows, max_k
+        self.inbox_bytes = ((max_rows * max_k * 4 + 255) // 256) * 256
+        self.nbytes = DATA_OFF + 2 * max(world, capacity_world or world) * self.inbox_bytes
         L = lib()
         with torch.cuda.device(device):
             ptr = ctypes.c_void_p()
@@ -64,7 +68,7 @@ class PeerGroup:
                 check(L.exl3_peer_open(ctypes.cast(h, ctypes.c_void_p), ctypes.byref(pp)), "exl3_peer_open")
                 desc.base[p] = pp.value
                 self.opened.append(pp.value)
-            desc.flag_off, desc.data_off, desc.slot_bytes = FLAG_OFF, DATA_OFF, self.slot_bytes
+            desc.flag_off, desc.data_off, desc.inbox_bytes = FLAG_OFF, DATA_OFF, self.inbox_bytes
             self.desc = desc
             self._raw = torch.as_tensor(_DevArray(self.own, self.nbytes), device=device)   # int16 view
         self.handle = bytes(handle)
@@ -73,15 +77,17 @@ class PeerGroup:
         """The own flag block as int32 words (tests)."""
         return self._raw[: 32].view(torch.int32)
 
-    def slot_view(self, slot: int, rows: int, k: int, dtype: torch.dtype) -> torch.Tensor:
-        """(rows, k) view of this rank's slot `slot` (where its GEMV writes the partial)."""
-        assert rows * k * 2 <= self.slot_bytes
-        off = (DATA_OFF + slot * self.slot_bytes) // 2
-        return self._raw[off: off + rows * k].view(dtype).view(rows, k)
+    def put(self, slot: int, src: torch.Tensor):
+        """Push this rank's (rows, k) 16-bit partial into inbox (slot, rank) of every rank (exl3_peer_put)."""
+        rows, k = src.shape
+        assert src.element_size() == 2 and src.is_contiguous()
+        check(lib().exl3_peer_put(ctypes.byref(self.desc), slot, src.data_ptr(), rows, k, stream_ptr(src.device)),
+              "exl3_peer_put")
 
-    def ar_add_norm_rot(self, slot: int, x: torch.Tensor, w: torch.Tensor, eps: float,
-                        suh: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """(h, xn, xh): h = x + sum over ranks of slot `slot`, xn = RMSNorm(h) * w, xh its rotations."""
+    def ar_add_norm_rot(self, slot: int, x: torch.Tensor, w: torch.Tensor, eps: float, suh: torch.Tensor,
+                        want_xn: bool = True) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
+        """(h, xn, xh): h = x + sum over ranks of this call's partials in slot `slot`, xn = RMSNorm(h) * w
+        (None unless want_xn), xh its rotations."""
         rows, k = x.shape
         suh = suh.reshape(-1, k)
         nm = suh.shape[0]
@@ -89,11 +95,12 @@ class PeerGroup:
         w = w.to(x.dtype).contiguous()
         suh = suh.to(torch.float16).contiguous()
         h = torch.empty_like(x)
-        xn = torch.empty_like(x)
+        xn = torch.empty_like(x) if want_xn else None
         xh = torch.empty((nm, rows, k), dtype=torch.float16, device=x.device)
         check(lib().exl3_ar_add_norm_rot(ctypes.byref(self.desc), slot, x.data_ptr(), w.data_ptr(),
                                          dtype_code(x.dtype), rows, k, float(eps), suh.data_ptr(), nm, h.data_ptr(),
-                                         xn.data_ptr(), xh.data_ptr(), stream_ptr(x.device)), "exl3_ar_add_norm_rot")
+                                         xn.data_ptr() if xn is not None else None, xh.data_ptr(),
+                                         stream_ptr(x.device)), "exl3_ar_add_norm_rot")
         return h, xn, xh
 
     def status(self) -> int:

@@ -32,6 +32,7 @@
 #include "exl3_b200.h"
 #include "exl3_common.cuh"
 #include "exl3_host.h"
+#include "exl3_peer.cuh"
 
 namespace exl3 {
 
@@ -49,6 +50,9 @@ struct GemvParams {
     long long units;
     int qkv;                 // 1: members are q, k, v and the finish is exl3_qkv_post's (no y)
     exl3_qkv_post_args post;
+    int ll_world;            // > 0: rows go as LL words into ll[0..ll_world) (exl3_gemv_peer; no y)
+    uint64_t* ll[8];         // inbox (slot, this rank) of every rank of the group
+    const uint32_t* epoch;   // own flag block's "last completed" epoch word
 };
 
 constexpr int kRedStride = 8 * 128;   // floats per warp partial (8 rows x 128 columns)
@@ -120,6 +124,30 @@ __device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half
     for (int i = 0; i < 4; ++i) {
         const int c = lane + 32 * i;
         yrow[c] = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
+    }
+}
+
+// Peer finish (exl3_gemv_peer): the row's values rounded to OT exactly as a stored y would be, pushed
+// as LL words (column pairs + the next all-reduce's epoch) into every rank's inbox. Even lanes pair
+// their column with the odd neighbour's.
+template <typename OT>
+__device__ __forceinline__ void finish_row_peer(float (&v)[4], int lane, const __half* svh, const GemvParams& p, int b,
+                                                int r)
+{
+    fwht128_rows(v, lane);
+    const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(p.epoch) + 1u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int c = lane + 32 * i;
+        const OT o = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
+        const uint32_t lo = *reinterpret_cast<const unsigned short*>(&o);
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, lo, 1);
+        if (!(lane & 1)) {
+            const size_t j = ((size_t)r * p.n_total + (size_t)b * 128 + c) >> 1;
+#pragma unroll
+            for (int d = 0; d < 8; ++d)
+                if (d < p.ll_world) st_ll(p.ll[d] + j, lo | (hi << 16), e);
+        }
     }
 }
 
@@ -406,6 +434,9 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
                 if (p.qkv) {
                     if (p.out_bf16) finish_qkv<__nv_bfloat16>(v, lane, sv, p, b, r);
                     else finish_qkv<__half>(v, lane, sv, p, b, r);
+                } else if (p.ll_world) {
+                    if (p.out_bf16) finish_row_peer<__nv_bfloat16>(v, lane, sv, p, b, r);
+                    else finish_row_peer<__half>(v, lane, sv, p, b, r);
                 } else if (p.out_bf16) {
                     finish_row(v, lane, sv, reinterpret_cast<__nv_bfloat16*>(p.y) + yoff);
                 } else {
@@ -568,12 +599,13 @@ extern "C" int exl3_gemv_reset(uint32_t* counters, size_t counter_bytes, void* s
 }
 
 static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
-                       void* y, float* partials, uint32_t* counters, const exl3_qkv_post_args* post, void* stream)
+                       void* y, float* partials, uint32_t* counters, const exl3_qkv_post_args* post,
+                       const exl3_peer_group* peer, int slot, void* stream)
 {
     using namespace exl3;
     GemvLaunch L;
     if (int e = plan_gemv(desc, &L)) return e;
-    if (!xh || !trellis || !svh || (!y && !post) || !partials || !counters) return EXL3_E_NULL;
+    if (!xh || !trellis || !svh || (!y && !post && !peer) || !partials || !counters) return EXL3_E_NULL;
     for (int m = 0; m < desc->n_members; ++m) {
         if (!trellis[m]) return EXL3_E_NULL;
         if (!aligned(trellis[m], 16)) return EXL3_E_ALIGN;
@@ -611,6 +643,14 @@ static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_
     prm.gran = L.gran;
     prm.qkv = post != nullptr;
     if (post) prm.post = *post;
+    if (peer) {
+        if (int e = check_peer_group(peer, slot)) return e;
+        if ((size_t)desc->rows * prm.n_total * 4 > peer->inbox_bytes) return EXL3_E_WORKSPACE;
+        prm.ll_world = peer->world;
+        for (int d = 0; d < 8; ++d)
+            prm.ll[d] = d < peer->world ? peer_inbox(peer->base[d], *peer, slot, peer->rank) : nullptr;
+        prm.epoch = peer_flags(peer->base[peer->rank], *peer) + kFlagEpoch;
+    }
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (desc->bits) {
@@ -685,7 +725,7 @@ extern "C" int exl3_gemv_noalloc(const exl3_gemv_desc* desc, const void* xh, con
 extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
                          void* y, float* partials, uint32_t* counters, void* stream)
 {
-    return gemv_common(desc, xh, trellis, svh, y, partials, counters, nullptr, stream);
+    return gemv_common(desc, xh, trellis, svh, y, partials, counters, nullptr, nullptr, 0, stream);
 }
 
 extern "C" int exl3_gemv_qkv_post(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
@@ -699,5 +739,13 @@ extern "C" int exl3_gemv_qkv_post(const exl3_gemv_desc* desc, const void* xh, co
     if (desc->n_members != 3 || post->hq < 1 || post->hkv < 1 || post->max_len < 1 || desc->n[0] != post->hq * 128 ||
         desc->n[1] != post->hkv * 128 || desc->n[2] != post->hkv * 128)
         return EXL3_E_SHAPE;
-    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, post, stream);
+    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, post, nullptr, 0, stream);
+}
+
+extern "C" int exl3_gemv_peer(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
+                              const void* svh, float* partials, uint32_t* counters, const exl3_peer_group* g, int slot,
+                              void* stream)
+{
+    if (!desc || !g) return EXL3_E_NULL;
+    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, nullptr, g, slot, stream);
 }

@@ -128,6 +128,20 @@ class TrellisGemvPlan:
                                        ctypes.byref(a), stream_ptr(xh.device)), "exl3_gemv_qkv_post")
         return q_out
 
+    def peer(self, xh: torch.Tensor, trellises: list[torch.Tensor], peers, slot: int) -> None:
+        """The GEMV with its output rows pushed into inbox (slot, rank) of every rank of `peers`
+        (comm.PeerGroup) for the next ar_add_norm_rot on that slot (exl3_gemv_peer); no y."""
+        assert len(trellises) == self.nsub
+        xh = xh.contiguous()
+        if xh.dtype != torch.float16 or xh.numel() != self.nsub * self.rows * self.k:
+            raise ValueError(f"xh must be fp16 ({self.nsub}, {self.rows}, {self.k})")
+        _need_cuda(xh, *trellises)
+        for i in range(3):
+            self._tptr[i] = trellises[i if i < self.nsub else 0].data_ptr()
+        check(lib().exl3_gemv_peer(ctypes.byref(self.desc), xh.data_ptr(), ctypes.cast(self._tptr, ctypes.c_void_p),
+                                   self.svh.data_ptr(), self.partials.data_ptr(), self.counters.data_ptr(),
+                                   ctypes.byref(peers.desc), slot, stream_ptr(xh.device)), "exl3_gemv_peer")
+
 
 def decode_wt(trellis_u32: torch.Tensor, k: int, n: int, K: int, cb: int, nt0: int = 0, ntc: int | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:

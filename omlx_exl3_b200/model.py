@@ -362,15 +362,14 @@ class Qwen3EXL3(nn.Module):
             nonlocal slot
             if peers is None:
                 return self.tp.all_reduce(lin.gemv_rotated(xh_in, dt))
-            out = peers.slot_view(slot, rows, hs, dt)
-            lin.plan(rows, dt)(xh_in, [lin._tr], out=out)
+            lin.plan(rows, dt).peer(xh_in, [lin._tr], peers, slot)   # pushed into every rank's inbox
             slot ^= 1
             return slot ^ 1
 
-        def add_norm(x, pend, w, suh):
+        def add_norm(x, pend, w, suh, want_xn=False):
             if peers is None:
-                return add_norm_rot(x, pend, w, eps, suh, want_xn=False)
-            return peers.ar_add_norm_rot(pend, x, w, eps, suh)
+                return add_norm_rot(x, pend, w, eps, suh, want_xn=want_xn)
+            return peers.ar_add_norm_rot(pend, x, w, eps, suh, want_xn=want_xn)
 
         for i, (layer, lp) in enumerate(zip(self.model.layers, self.__dict__["_decode_plans"])):
             attn = layer.self_attn
@@ -399,7 +398,8 @@ class Qwen3EXL3(nn.Module):
         w_out = self.model.norm.weight
         head = self.__dict__["_head_targets"]
         if head is None:
-            return add_norm(x, pending, w_out, torch.ones((1, hs), dtype=torch.float16, device=x.device))[1]
+            return add_norm(x, pending, w_out, torch.ones((1, hs), dtype=torch.float16, device=x.device),
+                            want_xn=True)[1]
         _, _, xh = add_norm(x, pending, w_out, head.suh)
         return head.outputs(xh, rows, dt)[0]
 
