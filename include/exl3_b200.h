@@ -205,6 +205,20 @@ EXL3_API int exl3_add_norm_rot(const void* x, const void* d, const void* w, int 
                                const void* suh, int n_members, void* x_out, void* xn, void* xh, void* stream);
 
 /*
+ * Decode attention fused with o_proj's input rotation, for rows new tokens (head_dim 128, GQA,
+ * rows * hq / hkv <= 16) over an fp16 KV cache:
+ *   xh[r, h*128 : h*128+128] = fp16( had128( fp16(softmax(q k^T / sqrt(128)) v) * suh[h*128 ..] ) / sqrt(128) )
+ * q: fp16 (rows, hq, 128); k_cache, v_cache: fp16 (hkv, max_len, 128), positions [0, T) valid, new
+ * row i at position T - rows + i sees positions <= that; suh: fp16 (hq * 128); xh: fp16 (rows, hq * 128).
+ * workspace: exl3_attn_workspace bytes, 16-byte aligned: 16 reserved bytes, then the split partials. Replaces: the model's
+ * scaled-dot-product attention + kernels.rot (src/omlx/exl3/kernels.py:451-458) of the decode step.
+ */
+EXL3_API int exl3_attn_workspace(int rows, int hq, int hkv, int max_len, int T, size_t* bytes);
+EXL3_API int exl3_attn_decode_rot(const void* q, const void* k_cache, const void* v_cache, int rows, int hq, int hkv,
+                                  int max_len, int T, const void* suh, void* xh, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/*
  * Tensor-parallel peer buffers (CUDA IPC over NVLink). Each rank of a tensor-parallel group creates
  * one buffer with exl3_peer_create (the one entry point that allocates device memory: the buffer
  * must be its own cudaMalloc allocation to be shared), sends the 64-byte handle to the other ranks

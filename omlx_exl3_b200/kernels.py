@@ -245,6 +245,43 @@ def qkv_post(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_w: torch.
     return q_out
 
 
+_ATTN_WS: dict = {}
+
+
+def attn_fits(rows: int, hq: int, hkv: int) -> bool:
+    """Whether attn_rot handles this shape (one m16 tile of q vectors per kv head)."""
+    return hq % hkv == 0 and rows * (hq // hkv) <= 16
+
+
+def attn_rot(q16: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, T: int, suh: torch.Tensor,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention of q16 (rows, hq, 128) fp16 over cache[:, :T] (causal among the new rows, which
+    sit at T - rows ..) fused with o_proj's input rotation: returns xh (1, rows, hq*128) fp16
+    (exl3_attn_decode_rot). The split scratch is one cached buffer per device, shared by calls that run
+    one after another on a stream."""
+    rows, hq = q16.shape[0], q16.shape[1]
+    hkv, max_len = k_cache.shape[0], k_cache.shape[1]
+    _need_cuda(q16, k_cache, v_cache, suh)
+    assert q16.dtype == k_cache.dtype == v_cache.dtype == torch.float16 and q16.shape[2] == 128
+    assert q16.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert tuple(v_cache.shape) == tuple(k_cache.shape) and k_cache.shape[2] == 128
+    suh = suh.to(torch.float16).reshape(-1).contiguous()
+    assert suh.numel() == hq * 128
+    nb = ctypes.c_size_t()
+    with torch.cuda.device(q16.device):
+        check(lib().exl3_attn_workspace(rows, hq, hkv, max_len, T, ctypes.byref(nb)), "exl3_attn_workspace")
+        key = q16.device.index
+        ws = _ATTN_WS.get(key)
+        if ws is None or ws.numel() * 4 < nb.value:
+            ws = torch.zeros(max(nb.value // 4 + 64, 1 << 16), dtype=torch.int32, device=q16.device)
+            _ATTN_WS[key] = ws
+    xh = out if out is not None else torch.empty((1, rows, hq * 128), dtype=torch.float16, device=q16.device)
+    check(lib().exl3_attn_decode_rot(q16.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), rows, hq, hkv, max_len,
+                                     int(T), suh.data_ptr(), xh.data_ptr(), ws.data_ptr(), nb.value,
+                                     stream_ptr(q16.device)), "exl3_attn_decode_rot")
+    return xh
+
+
 def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float, suh: torch.Tensor,
                  want_xn: bool = True) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
     """h = x + d, RMSNorm(h) * w (MLX rounding) and its rotations: returns (h, xn, xh (NM, rows, K) fp16);

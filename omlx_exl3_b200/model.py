@@ -22,7 +22,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
-from .kernels import MAX_GEMV_ROWS, add_norm_rot, norm_rot, qkv_post, rot, swiglu_rot
+from .kernels import MAX_GEMV_ROWS, add_norm_rot, attn_fits, attn_rot, norm_rot, qkv_post, rot, swiglu_rot
 from .linear import EXL3Linear
 
 
@@ -387,8 +387,11 @@ class Qwen3EXL3(nn.Module):
                 outs = lp.qkv.outputs(xh, rows, dt)
                 q16 = qkv_post(_cols(outs, lp.qkv_at[0]), _cols(outs, lp.qkv_at[1]), _cols(outs, lp.qkv_at[2]),
                                attn.q_norm.weight, attn.k_norm.weight, eps, self.rope_cos, self.rope_sin, pos, kc, vc)
-            o = self._attend(q16, kc, vc, T, rows)
-            a = row_parallel(attn.o_proj, rot(o, attn.o_proj.rot_suh))
+            if attn_fits(rows, q16.shape[1], kc.shape[0]):     # attention fused with o_proj's input rotation
+                xo = attn_rot(q16, kc, vc, T, attn.o_proj.rot_suh)
+            else:
+                xo = rot(self._attend(q16, kc, vc, T, rows), attn.o_proj.rot_suh)
+            a = row_parallel(attn.o_proj, xo)
             x, _, xh = add_norm(x, a, layer.post_attention_layernorm.weight, lp.gate_up.suh)
             gu_outs = lp.gate_up.outputs(xh, rows, torch.float16)
             gu = gu_outs[0] if len(gu_outs) == 1 else torch.cat(
