@@ -1,457 +1,18 @@
-// EXL3 decode GEMV (1..8 rows) for sm_100a: y = had128(xh @ W) / sqrt(128) * svh in one launch.
-//
-// Replaces the reference's trellis GEMV (daig/omlx-exl3 src/omlx/exl3/kernels.py:114-299).
-//
-// Work split (stream-K over "units"): a unit is one 16-row k-slice of one 128-column output block,
-// i.e. 8 consecutive trellis tiles = 256*K contiguous bytes. Units are numbered block-major
-// (u = block * KT + kt) and each persistent CTA (one per SM) owns the contiguous range
-// [c*U/G, (c+1)*U/G), so every SM streams the same number of bytes whatever the shape.
-//
-// Inside a CTA every warp streams its own units (CTA unit indices w, w + NCW, ...) into a private
-// shared-memory ring with 16-byte cp.async copies, DEPTH - 1 units ahead of the unit it decodes (no
-// producer thread and no cross-warp handshake: many small copies from all warps keep enough bytes in
-// flight). A warp decodes each of the unit's 8 tiles straight into m16n8k16 A fragments (one lane =
-// 8 consecutive stream positions, exl3_common.cuh) and, for 2..8 rows, issues two MMAs per tile
-// against the rows of xh duplicated across each k pair ("split" operands: the 3inst/mcg weight is
-// the sum of two fp16 halves, so A = (lo, hi) and B = (x, x)); accumulators are fp32 registers.
-// For one row the same split words are multiplied on the CUDA cores instead (half2 FMA against
-// (x, x), flushed to fp32 every few units), which avoids the legacy MMA issue limit.
-//
-// Reduction, fixed order (bitwise reproducible, row-exact): at the end of each block segment the
-// consumer warps sum their accumulators through shared memory in warp order. A block that lies
-// entirely inside one CTA is finished right there; otherwise each CTA publishes its partial, and
-// the last CTA to arrive (per-block arrival counter, zero at rest) sums the partials in CTA order.
-// The finishing CTA applies the 128-point FWHT (Sylvester order, stages 1..64 as the reference),
-// * 1/sqrt(128) * svh, and writes y in the output dtype. No CTA ever waits on another CTA.
+// EXL3 decode GEMV: grid planner and C entry points (exl3_gemv, exl3_gemv_noalloc, exl3_gemv_qkv_post,
+// exl3_gemv_peer). The kernel and its design notes are in exl3_gemv_kernel.cuh.
 #include <cuda_runtime.h>
 
 #include <map>
 #include <mutex>
 #include <tuple>
 
-#include "exl3_b200.h"
-#include "exl3_common.cuh"
-#include "exl3_host.h"
-#include "exl3_peer.cuh"
+#include "exl3_gemv_kernel.cuh"
 
 namespace exl3 {
 
-struct GemvParams {
-    const uint32_t* trellis[3];
-    int nt_member[3];        // n-tiles of each member (row stride of its trellis, in tiles)
-    int blk_off[4];          // first global 128-column block of each member; [nm] = total blocks
-    int nm;
-    const __half* xh;        // (nm, rows, k)
-    const __half* svh;       // (n_total)
-    void* y;                 // (rows, n_total)
-    float* partials;         // grid * J * 8 * 128
-    uint32_t* counters;      // blocks, then one status word
-    int k, KT, rows, n_total, blocks, out_bf16, J, row_exact, gran;
-    long long units;
-    int qkv;                 // 1: members are q, k, v and the finish is exl3_qkv_post's (no y)
-    exl3_qkv_post_args post;
-    int ll_world;            // > 0: rows go as LL words into ll[0..ll_world) (exl3_gemv_peer; no y)
-    uint64_t* ll[8];         // inbox (slot, this rank) of every rank of the group
-    const uint32_t* epoch;   // own flag block's "last completed" epoch word
-};
-
-constexpr int kRedStride = 8 * 128;   // floats per warp partial (8 rows x 128 columns)
-// rows == 1: the half2 accumulators take kFlush units (4 products per half each) before they are
-// added into fp32, which bounds the fp16 accumulation to 16 products
-constexpr int kFlush = 4;
-
-template <int K, int NCW>
-struct GemvShape {
-    static constexpr int TW = 8 * K;                 // words per tile
-    static constexpr int UW = 8 * TW;                // words per unit (8 tiles)
-    static constexpr int UB = UW * 4;                // bytes per unit
-    static constexpr int D0 = (96 * 1024) / (NCW * UB);
-    static constexpr int DEPTH = D0 < 3 ? 3 : (D0 > 8 ? 8 : D0);   // units in flight per warp
-    static constexpr int RING = NCW * DEPTH * UB;
-    static constexpr int RED = NCW * kRedStride * 4;
-    static constexpr int SMEM = RING + RED;
-    static constexpr int THREADS = 32 * NCW;
-};
-
-// 32-bit: the host guarantees units * (grid + 1) < 2^32
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(uint32_t* p, unsigned v)
-{
-    unsigned old;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-
-__device__ __forceinline__ int owner_cta(unsigned u, unsigned U, unsigned G)
-{
-    return (int)(((u + 1) * G - 1) / U);
-}
-
-__device__ __forceinline__ int cta_start(unsigned c, unsigned U, unsigned G)
-{
-    return (int)(c * U / G);
-}
-
-// 128-point FWHT of one row held by one warp as v[i] = column lane + 32 i, then scale, svh, store.
-__device__ __forceinline__ void fwht128_rows(float (&v)[4], int lane)
-{
-#pragma unroll
-    for (int h = 1; h < 32; h <<= 1) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float p = __shfl_xor_sync(0xffffffffu, v[i], h);
-            v[i] = (lane & h) ? p - v[i] : v[i] + p;
-        }
-    }
-    {   // h = 32: columns c, c + 32 are v[i], v[i + 1] for i even
-        float a0 = v[0], a1 = v[1];
-        v[0] = a0 + a1; v[1] = a0 - a1;
-        a0 = v[2]; a1 = v[3];
-        v[2] = a0 + a1; v[3] = a0 - a1;
-    }
-    {   // h = 64
-        float a0 = v[0], a1 = v[2];
-        v[0] = a0 + a1; v[2] = a0 - a1;
-        a0 = v[1]; a1 = v[3];
-        v[1] = a0 + a1; v[3] = a0 - a1;
-    }
-}
-
-template <typename OT>
-__device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half* svh, OT* yrow)
-{
-    fwht128_rows(v, lane);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = lane + 32 * i;
-        yrow[c] = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
-    }
-}
-
-// Peer finish (exl3_gemv_peer): the row's values rounded to OT exactly as a stored y would be, pushed
-// as LL words (column pairs + the next all-reduce's epoch) into every rank's inbox. Even lanes pair
-// their column with the odd neighbour's.
-template <typename OT>
-__device__ __forceinline__ void finish_row_peer(float (&v)[4], int lane, const __half* svh, const GemvParams& p, int b,
-                                                int r)
-{
-    fwht128_rows(v, lane);
-    const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(p.epoch) + 1u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = lane + 32 * i;
-        const OT o = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
-        const uint32_t lo = *reinterpret_cast<const unsigned short*>(&o);
-        const uint32_t hi = __shfl_down_sync(0xffffffffu, lo, 1);
-        if (!(lane & 1)) {
-            const size_t j = ((size_t)r * p.n_total + (size_t)b * 128 + c) >> 1;
-#pragma unroll
-            for (int d = 0; d < 8; ++d)
-                if (d < p.ll_world) st_ll(p.ll[d] + j, lo | (hi << 16), e);
-        }
-    }
-}
-
-// The q/k/v group's finish, fused with exl3_qkv_post: block b is one head of q (member 0), k (1) or
-// v (2). The GEMV value is rounded to the model dtype T exactly as a stored y would be, then q/k get
-// the per-head RMSNorm (MLX rounding) and rotate-half RoPE and go to q_out / the k cache, v to the v
-// cache, all at this row's position.
-template <typename T>
-__device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const __half* svh, const GemvParams& p, int b,
-                                           int r)
-{
-    fwht128_rows(v, lane);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = to_f32(from_f32<T>(v[i] * kHadScale * __half2float(svh[lane + 32 * i])));
-    const exl3_qkv_post_args& a = p.post;
-    const int m = b >= p.blk_off[2] ? 2 : (b >= p.blk_off[1] ? 1 : 0);
-    const int head = b - (m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]));
-    const long long pos = a.pos[r];
-    const float* cs = a.cos_table + (size_t)pos * 64;
-    const float* sn = a.sin_table + (size_t)pos * 64;
-    __half* o;
-    if (m == 0) {
-        head_rms<T>(v, static_cast<const T*>(a.q_norm_w), a.eps, lane);
-        rope_half(v, cs, sn, lane);
-        o = static_cast<__half*>(a.q_out) + ((size_t)r * a.hq + head) * 128;
-    } else if (m == 1) {
-        head_rms<T>(v, static_cast<const T*>(a.k_norm_w), a.eps, lane);
-        rope_half(v, cs, sn, lane);
-        o = static_cast<__half*>(a.k_cache) + ((size_t)head * a.max_len + pos) * 128;
-    } else {
-        o = static_cast<__half*>(a.v_cache) + ((size_t)head * a.max_len + pos) * 128;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[lane + 32 * i] = __float2half_rn(m == 2 ? v[i] : to_f32(from_f32<T>(v[i])));
-}
-
-template <int K, int CB, int NCW, bool ROWS1>
-__global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
-{
-    using S = GemvShape<K, NCW>;
-    extern __shared__ __align__(128) uint8_t smem[];
-    float* red = reinterpret_cast<float*>(smem + S::RING);
-    __shared__ int s_last;
-
-    const int lane = threadIdx.x & 31;
-    const int cw = threadIdx.x >> 5;
-    const int ctid = threadIdx.x;
-    const int G = gridDim.x, c = blockIdx.x;
-    // CTA ranges are whole granules of p.gran units (16 when k is a multiple of 256), so every block
-    // segment inside a CTA is a whole number of rounds of the NCW warps
-    const int gran = p.gran;
-    const unsigned U = (unsigned)(p.units / gran);
-    const int u0 = cta_start(c, U, G) * gran, u1 = cta_start(c + 1, U, G) * gran;
-    const int n_units = (int)(u1 - u0);
-    const int KT = p.KT;
-    const int rows = p.rows;
-    const int b_first = (int)(u0 / KT), b_last = (int)((u1 - 1) / KT);
-
-    // Every warp streams its own units (CTA unit indices cw, cw + NCW, ...) into a private ring of
-    // DEPTH slots with 16-byte cp.async copies, DEPTH - 1 units ahead of the one it decodes. The
-    // source pointer (already offset by this lane's first chunk) advances by a fixed stride while
-    // the warp stays inside one 128-column block and is recomputed only when it moves to the next.
-    constexpr int kChunks = S::UB / 16;                               // 16-byte chunks per unit
-    constexpr int kPerLane = (kChunks + 31) / 32;
-    uint32_t* wring = reinterpret_cast<uint32_t*>(smem) + (size_t)cw * S::DEPTH * S::UW + lane * 4;
-    int fi = cw;                                                      // next unit index to fetch
-    int fb = 0, fkt = 0;
-    const uint32_t* fsrc = nullptr;
-    size_t fstep = 0;                                                 // words between k-slices NCW apart
-    auto fseek = [&]() {
-        const int u = u0 + fi;
-        fb = (int)(u / KT);
-        fkt = u - fb * KT;
-        const int m = (p.nm > 1 && fb >= p.blk_off[1]) ? ((p.nm > 2 && fb >= p.blk_off[2]) ? 2 : 1) : 0;
-        const int ntm = m == 0 ? p.nt_member[0] : (m == 1 ? p.nt_member[1] : p.nt_member[2]);
-        const int off = m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]);
-        const uint32_t* base = m == 0 ? p.trellis[0] : (m == 1 ? p.trellis[1] : p.trellis[2]);
-        fsrc = base + ((size_t)fkt * ntm + (size_t)(fb - off) * 8) * S::TW + lane * 4;
-        fstep = (size_t)NCW * ntm * S::TW;
-    };
-    if (fi < n_units) fseek();
-    int fslot = 0;
-    auto fetch = [&]() {
-        if (fi < n_units) {
-            uint32_t* dst = wring + (size_t)fslot * S::UW;
-#pragma unroll
-            for (int cidx = 0; cidx < kPerLane; ++cidx)
-                if (kChunks % 32 == 0 || cidx * 32 + lane < kChunks) cp_async16(dst + cidx * 128, fsrc + cidx * 128);
-            fi += NCW;
-            fkt += NCW;
-            if (fkt >= KT) {
-                if (fi < n_units) fseek();
-            } else {
-                fsrc += fstep;
-            }
-        }
-        cp_async_commit();                                    // (possibly empty) group per unit
-        fslot = fslot + 1 == S::DEPTH ? 0 : fslot + 1;
-    };
-#pragma unroll 1
-    for (int d = 0; d < S::DEPTH - 1; ++d) fetch();
-    // The weights are constant; everything from here on (xh, y, the split-k scratch) may be written or
-    // read by the previous kernel in the stream, so under programmatic dependent launch the ring fill
-    // above overlaps that kernel and the rest waits for it.
-    pdl_trigger();
-    pdl_wait();
-    int cslot = 0;                                            // ring slot of the unit being decoded
-
-    const int g = lane >> 2, q = lane & 3;
-    const LaneWindow<K> lw(lane);
-    const HashRegs hr = hash_regs<CB>();
-    const bool xlane = ROWS1 || g < rows;         // this lane carries a row of xh
-
-    for (int b = b_first; b <= b_last; ++b) {
-        const int m = (p.nm > 1 && b >= p.blk_off[1]) ? ((p.nm > 2 && b >= p.blk_off[2]) ? 2 : 1) : 0;
-        const __half* xrow = p.xh + ((size_t)m * rows + (ROWS1 ? 0 : g)) * p.k;
-        const int sa = max(u0, b * KT) - u0;
-        const int se = min(u1, (b + 1) * KT) - u0;
-
-        // MMA path: acc[j] = the m16n8 accumulator of tile j. rows == 1 path: acc[j][0] / [1] are
-        // columns g / g+8 of tile j in fp32, fed from half2 accumulators hacc every kFlush units.
-        float acc[8][4];
-        __half2 hacc[8][2];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-            hacc[j][0] = hacc[j][1] = __float2half2_rn(0.f);
-        }
-        int since_flush = 0;
-
-        const int kt_base = u0 - b * KT;                     // k-slice of unit index 0 (may be < 0)
-        int i = sa + ((cw - sa) % NCW + NCW) % NCW;
-        // the lane's xh values for the next unit are fetched one unit ahead
-        const __half* xp = xrow + (kt_base + i) * 16 + 2 * q;
-        uint32_t x0n = 0, x1n = 0;
-        if (i < se && xlane) {
-            x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
-            x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
-        }
-        for (; i < se; i += NCW) {
-            const uint32_t x0 = x0n, x1 = x1n;
-            xp += NCW * 16;
-            if (i + NCW < se && xlane) {
-                x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
-                x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
-            }
-            // x duplicated across each k pair: (x[2q], x[2q]), (x[2q+8], ..), (x[2q+1], ..), (x[2q+9], ..)
-            const uint32_t be0 = prmt(x0, x0, 0x1010), be1 = prmt(x1, x1, 0x1010);
-            const uint32_t bo0 = prmt(x0, x0, 0x3232), bo1 = prmt(x1, x1, 0x3232);
-            fetch();                                  // unit + DEPTH - 1 (or an empty group)
-            cp_async_wait<S::DEPTH - 1>();            // this unit's copies have landed
-            __syncwarp();
-            const uint32_t* unit = wring - lane * 4 + (size_t)cslot * S::UW;
-            cslot = cslot + 1 == S::DEPTH ? 0 : cslot + 1;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                uint32_t w[3], h[8], a[8];
-                window_words<K>(unit + j * S::TW, lw, w);
-                hashes8<K, CB>(w, h, hr);
-#pragma unroll
-                for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t], hr);
-                if constexpr (ROWS1) {
-                    // columns g (positions 0..3) and g+8 (4..7); k 2q, 2q+1, 2q+8, 2q+9
-                    const __half2 xe0 = *reinterpret_cast<const __half2*>(&be0);
-                    const __half2 xo0 = *reinterpret_cast<const __half2*>(&bo0);
-                    const __half2 xe1 = *reinterpret_cast<const __half2*>(&be1);
-                    const __half2 xo1 = *reinterpret_cast<const __half2*>(&bo1);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[0]), xe0, hacc[j][0]);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[1]), xo0, hacc[j][0]);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[2]), xe1, hacc[j][0]);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[3]), xo1, hacc[j][0]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[4]), xe0, hacc[j][1]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[5]), xo0, hacc[j][1]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[6]), xe1, hacc[j][1]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[7]), xo1, hacc[j][1]);
-                } else {
-                    // even k of the tile: (g,2q) (g+8,2q) (g,2q+8) (g+8,2q+8); odd k: the +1 neighbours
-                    mma16816(acc[j], a[0], a[4], a[2], a[6], be0, be1);
-                    mma16816(acc[j], a[1], a[5], a[3], a[7], bo0, bo1);
-                }
-            }
-            __syncwarp();                             // the slot is refilled by the next fetch
-            if constexpr (ROWS1) {
-                if (++since_flush == kFlush) {
-                    since_flush = 0;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-#pragma unroll
-                        for (int cc = 0; cc < 2; ++cc) {
-                            const float2 f = __half22float2(hacc[j][cc]);
-                            acc[j][cc] += f.x + f.y;
-                            hacc[j][cc] = __float2half2_rn(0.f);
-                        }
-                }
-            }
-        }
-
-        // ---- segment end: warp partials -> shared memory, summed in warp order
-        float* rw = red + cw * kRedStride;
-        if constexpr (ROWS1) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const float2 f = __half22float2(hacc[j][cc]);
-                    float v = acc[j][cc] + (f.x + f.y);
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);     // the 4 lanes of column g
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    if (q == 0) rw[16 * j + g + 8 * cc] = v;
-                }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int col = 16 * j + g;
-                if (2 * q < rows) {
-                    rw[(2 * q) * 128 + col] = acc[j][0];
-                    rw[(2 * q) * 128 + col + 8] = acc[j][2];
-                }
-                if (2 * q + 1 < rows) {
-                    rw[(2 * q + 1) * 128 + col] = acc[j][1];
-                    rw[(2 * q + 1) * 128 + col + 8] = acc[j][3];
-                }
-            }
-        }
-        __syncthreads();
-        for (int e = ctid; e < rows * 128; e += 32 * NCW) {
-            float v = red[e];
-#pragma unroll
-            for (int w = 1; w < NCW; ++w) v += red[w * kRedStride + e];
-            red[e] = v;
-        }
-        __syncthreads();
-
-        const bool whole = b * KT >= u0 && (b + 1) * KT <= u1;
-        bool finish = whole;
-        if (!whole) {
-            // one warp publishes the CTA's partial and takes the block's arrival ticket
-            if (cw == 0) {
-                float* gp = p.partials + ((size_t)c * p.J + (b - b_first)) * kRedStride;
-                for (int e = lane; e < rows * 128; e += 32) gp[e] = red[e];
-                __syncwarp();                                // the warp's stores, ordered before lane 0's release
-                if (lane == 0) {
-                    const int c_first = owner_cta(b * KT / gran, U, G);
-                    const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
-                    // one acquire-release RMW: publishes this CTA's partial and, for the last arriver,
-                    // makes every other CTA's partial visible (no separate fences)
-                    const unsigned old = atom_add_acq_rel_gpu(&p.counters[b], 1u);
-                    s_last = old == (unsigned)(c_last - c_first);
-                }
-            }
-            __syncthreads();
-            finish = s_last != 0;
-            if (finish) {
-                const int c_first = owner_cta(b * KT / gran, U, G);
-                const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
-                // CTA c_first holds the block in its slot jj0, every later CTA in its slot 0. The loads
-                // go out in batches of 8 before any add (an add per load would serialise the L2
-                // round trips); the adds stay in CTA order.
-                const int jj0 = b - (int)(cta_start(c_first, U, G) * gran / KT);
-                for (int e = ctid; e < rows * 128; e += 32 * NCW) {
-                    float v = __ldcg(p.partials + ((size_t)c_first * p.J + jj0) * kRedStride + e);
-                    for (int cc = c_first + 1; cc <= c_last; cc += 8) {
-                        float t[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            t[i] = cc + i <= c_last ? __ldcg(p.partials + (size_t)(cc + i) * p.J * kRedStride + e) : 0.f;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            if (cc + i <= c_last) v += t[i];
-                    }
-                    red[e] = v;
-                }
-                if (ctid == 0) atomicExch(&p.counters[b], 0u);
-                __syncthreads();
-            }
-        }
-        if (finish) {
-            for (int r = cw; r < rows; r += NCW) {
-                float v[4];
-#pragma unroll
-                for (int ii = 0; ii < 4; ++ii) v[ii] = red[r * 128 + lane + 32 * ii];
-                const __half* sv = p.svh + (size_t)b * 128;
-                const size_t yoff = (size_t)r * p.n_total + (size_t)b * 128;
-                if (p.qkv) {
-                    if (p.out_bf16) finish_qkv<__nv_bfloat16>(v, lane, sv, p, b, r);
-                    else finish_qkv<__half>(v, lane, sv, p, b, r);
-                } else if (p.ll_world) {
-                    if (p.out_bf16) finish_row_peer<__nv_bfloat16>(v, lane, sv, p, b, r);
-                    else finish_row_peer<__half>(v, lane, sv, p, b, r);
-                } else if (p.out_bf16) {
-                    finish_row(v, lane, sv, reinterpret_cast<__nv_bfloat16*>(p.y) + yoff);
-                } else {
-                    finish_row(v, lane, sv, reinterpret_cast<__half*>(p.y) + yoff);
-                }
-            }
-        }
-        __syncthreads();   // red is reused by the next segment
-    }
-}
-
+template int launch_gemv_epi<0>(int, int, const GemvParams&, int, cudaStream_t);
 
 // ---------------------------------------------------------------------------------------- host
-
-constexpr int kNCW = 16;
 
 struct GemvLaunch {
     int grid, J, blocks, KT, gran;
@@ -544,40 +105,6 @@ static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
     return EXL3_OK;
 }
 
-template <int K, int CB, bool ROWS1>
-static int launch_gemv_v(const GemvParams& prm, int grid, cudaStream_t s)
-{
-    using S = GemvShape<K, kNCW>;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemv_kernel<K, CB, kNCW, ROWS1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 S::SMEM) != cudaSuccess)
-            return EXL3_E_CUDA;
-        attr_set[dev] = true;
-    }
-    if (int e_ = launch_pdl(gemv_kernel<K, CB, kNCW, ROWS1>, grid, S::THREADS, S::SMEM, s, prm)) return e_;
-    return launch_status();
-}
-
-template <int K, int CB>
-static int launch_gemv_k(const GemvParams& prm, int grid, cudaStream_t s)
-{
-    return prm.rows == 1 && !prm.row_exact ? launch_gemv_v<K, CB, true>(prm, grid, s)
-                                           : launch_gemv_v<K, CB, false>(prm, grid, s);
-}
-
-template <int K>
-static int launch_gemv_cb(int cb, const GemvParams& prm, int grid, cudaStream_t s)
-{
-    switch (cb) {
-    case 0: return launch_gemv_k<K, 0>(prm, grid, s);
-    case 1: return launch_gemv_k<K, 1>(prm, grid, s);
-    default: return launch_gemv_k<K, 2>(prm, grid, s);
-    }
-}
-
 }  // namespace exl3
 
 extern "C" int exl3_gemv_workspace(const exl3_gemv_desc* desc, size_t* partial_bytes, size_t* counter_bytes)
@@ -641,7 +168,6 @@ static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_
     prm.row_exact = (desc->flags & EXL3_GEMV_ROW_EXACT) != 0;
     prm.units = L.units;
     prm.gran = L.gran;
-    prm.qkv = post != nullptr;
     if (post) prm.post = *post;
     if (peer) {
         if (int e = check_peer_group(peer, slot)) return e;
@@ -653,16 +179,9 @@ static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_
     }
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    switch (desc->bits) {
-    case 1: return launch_gemv_cb<1>(desc->codebook, prm, L.grid, s);
-    case 2: return launch_gemv_cb<2>(desc->codebook, prm, L.grid, s);
-    case 3: return launch_gemv_cb<3>(desc->codebook, prm, L.grid, s);
-    case 4: return launch_gemv_cb<4>(desc->codebook, prm, L.grid, s);
-    case 5: return launch_gemv_cb<5>(desc->codebook, prm, L.grid, s);
-    case 6: return launch_gemv_cb<6>(desc->codebook, prm, L.grid, s);
-    case 7: return launch_gemv_cb<7>(desc->codebook, prm, L.grid, s);
-    default: return launch_gemv_cb<8>(desc->codebook, prm, L.grid, s);
-    }
+    if (post) return launch_gemv_epi<1>(desc->bits, desc->codebook, prm, L.grid, s);
+    if (peer) return launch_gemv_epi<2>(desc->bits, desc->codebook, prm, L.grid, s);
+    return launch_gemv_epi<0>(desc->bits, desc->codebook, prm, L.grid, s);
 }
 
 // ---------------------------------------------------------------------------------------- no-alloc
