@@ -324,6 +324,7 @@ def run_prefill(args, local_rank):
     import torch
 
     from omlx_exl3_b200 import kernels
+    from omlx_exl3_b200.prefill import use_fused
 
     dev = torch.device("cuda", local_rank)
     gen = torch.Generator(device=dev)
@@ -348,7 +349,8 @@ def run_prefill(args, local_rank):
                 torch.matmul(xh, wt.t(), out=yh)
                 kernels.had_svh(yh, svh, torch.bfloat16)
 
-            res = {"M": M, "k": k, "n": n, "bits": K}
+            res = {"M": M, "k": k, "n": n, "bits": K,
+                   "default": "fused_tcgen05" if use_fused(M, n) else "decode_once_gemm"}
             for name, fn in (("fused_tcgen05", fused), ("decode_once_gemm", decode_once)):
                 for _ in range(3):
                     fn()

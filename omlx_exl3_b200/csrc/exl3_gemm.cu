@@ -5,17 +5,19 @@
 // of 16384-column chunks to fp16 in memory, MLX matmul, _had128, * svh). Here nothing but xh, the
 // trellis and y touch HBM.
 //
-// CTA tile: 256 rows of xh (two M=128 halves) x 128 output columns (one Hadamard block) x the whole k,
-// in k-steps of 64. Per k-step and pipeline stage:
-//   - warp 0 (one lane) loads the 256 x 64 fp16 xh tile with one TMA tensor load (128B swizzle);
-//   - warps 2..9 decode the 4 x 8 trellis tiles of the step (16 k-rows x 16 columns each; one lane =
+// CTA tile: BM rows of xh (BM / 128 M=128 accumulators: 256 rows for M <= 256, else 512) x 128 output
+// columns (one Hadamard block) x the whole k, in k-steps of 64. Per k-step and pipeline stage:
+//   - warp 0 (one lane) loads the BM x 64 fp16 xh tile with TMA tensor loads of 256 rows (128B swizzle);
+//   - warps 2..17 decode the 4 x 8 trellis tiles of the step (16 k-rows x 16 columns each; one lane =
 //     8 consecutive stream positions, exl3_common.cuh) to exact fp16 weights and store them straight
 //     into the 128 x 64 B tile in the same K-major 128B-swizzled layout the tensor core reads;
-//   - warp 1 (one lane) issues 2 x 4 tcgen05.mma (M=128, N=128, K=16, fp16 in, fp32 accumulate in
-//     tensor memory) and commits them to the stage's "empty" barrier.
-// The epilogue warps (2..9) read one accumulator row per thread (tcgen05.ld 32x32b: 128 fp32 columns),
-// run the 128-point FWHT in registers (stage order 1..64, as the reference), scale by 1/sqrt(128) and
-// svh, and store y. Every wait is bounded (exl3_common.cuh mbar_wait): a lost completion sets a status
+//   - warp 1 (one lane) issues BM / 128 x 4 tcgen05.mma (M=128, N=128, K=16, fp16 in, fp32 accumulate
+//     in tensor memory) and commits them to the stage's "empty" barrier.
+// The weight decode is the kernel's bound, so a taller row tile serves more MMAs per decoded tile: at
+// BM = 512 each weight of an M <= 512 GEMM is decoded once, and the 512 TMEM columns hold the four
+// accumulators. The epilogue warps read one accumulator row half per thread (tcgen05.ld 32x32b), run
+// the 128-point FWHT in registers (stage order 1..64, as the reference), scale by 1/sqrt(128) and svh,
+// and store y. Every wait is bounded (exl3_common.cuh mbar_wait): a lost completion sets a status
 // bit instead of hanging.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -30,18 +32,25 @@
 
 namespace exl3 {
 
-constexpr int kGemmBM = 256;                  // rows of xh per CTA (two M=128 MMAs)
 constexpr int kGemmBN = 128;                  // output columns per CTA
 constexpr int kGemmBK = 64;                   // k per pipeline stage (128 bytes of fp16: one swizzle row)
-constexpr int kGemmStages = 3;
 constexpr int kGemmDecWarps = 16;
 constexpr int kGemmThreads = 32 * (2 + kGemmDecWarps);
-constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;   // 32 KB
 constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;   // 16 KB
 constexpr int kGemmDecDepth = 4;              // trellis k-steps in flight per decoder warp
-// + per decoder warp a ring of kGemmDecDepth x 4 tiles x 32K bytes (K <= 8: 256 bytes per tile)
-constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmABytes + kGemmBBytes) + 256 + kGemmDecWarps * kGemmDecDepth * 2 * 256;
-static_assert(kGemmBM * 129 * 4 <= kGemmStages * (kGemmABytes + kGemmBBytes), "epilogue exchange buffer");
+
+// BM rows per CTA: shared memory = operand stages + barriers + per decoder warp a ring of
+// kGemmDecDepth x 2 tiles x 32 K bytes (K <= 8: 256 bytes per tile)
+template <int BM>
+struct GemmTile {
+    static constexpr int NH = BM / 128;                           // M=128 accumulators
+    static constexpr int STAGES = BM == 512 ? 2 : 3;
+    static constexpr int ABYTES = BM * kGemmBK * 2;              // 32 or 64 KB
+    static constexpr int SMEM = 1024 + STAGES * (ABYTES + kGemmBBytes) + 256 + kGemmDecWarps * kGemmDecDepth * 2 * 256;
+    static constexpr int TMEM_COLS = NH * kGemmBN;
+    static_assert(256 * 129 * 4 <= STAGES * (ABYTES + kGemmBBytes), "epilogue exchange buffer");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
 
 struct GemmParams {
     const uint32_t* trellis;
@@ -93,12 +102,15 @@ __device__ __forceinline__ void store_row64(OT* dst, const float (&v)[64], const
     }
 }
 
-template <int K, int CB>
+template <int K, int CB, int BM>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p)
 {
+    using TL = GemmTile<BM>;
+    constexpr int kGemmStages = TL::STAGES;
+    constexpr int kGemmABytes = TL::ABYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* As = smem;                                         // stages x 32 KB
+    uint8_t* As = smem;                                         // stages x BM x 128 bytes
     uint8_t* Bs = smem + kGemmStages * kGemmABytes;             // stages x 16 KB
     uint64_t* bars = reinterpret_cast<uint64_t*>(Bs + kGemmStages * kGemmBBytes);
     uint64_t* full = bars;                                      // xh tile landed
@@ -110,7 +122,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     constexpr int TW = 8 * K;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = blockIdx.x;                                  // 128-column block
-    const int m0 = blockIdx.y * kGemmBM;
+    const int m0 = blockIdx.y * BM;
     const int nsteps = p.k / kGemmBK;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGemmStages; ++s) {
@@ -122,8 +134,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        // 256 TMEM columns: two 128 x 128 fp32 accumulators
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tmem_slot)));
+        // NH x 128 TMEM columns: the 128 x 128 fp32 accumulators
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "n"(TL::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -142,7 +155,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], kGemmABytes);
-                tma_load_2d(As + s * kGemmABytes, &xmap, i * kGemmBK, m0, &full[s]);
+#pragma unroll
+                for (int t = 0; t < BM / 256; ++t)                // boxes of 256 rows
+                    tma_load_2d(As + s * kGemmABytes + t * 256 * 128, &xmap, i * kGemmBK, m0 + 256 * t, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -163,8 +178,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 for (int kk = 0; kk < kGemmBK / 16; ++kk) {
                     const uint64_t bdesc = smem_desc_sw128(Bs + s * kGemmBBytes + kk * 32);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint64_t adesc = smem_desc_sw128(As + s * kGemmABytes + h * (kGemmABytes / 2) + kk * 32);
+                    for (int h = 0; h < TL::NH; ++h) {
+                        const uint64_t adesc = smem_desc_sw128(As + s * kGemmABytes + h * 128 * 128 + kk * 32);
                         tc_mma_f16(tmem + h * kGemmBN, adesc, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
                     }
                 }
@@ -239,55 +254,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         }
         cp_async_wait<0>();                                     // no copy in flight past this point
 
-        // ---- epilogue: each thread takes 64 columns of one accumulator row; the 16 decoder warps
-        // cover (M half, column half) x the 4 TMEM lane quarters
+        // ---- epilogue: each thread takes 64 columns of one accumulator row; per pass the 16 decoder
+        // warps cover (two accumulators, column half) x the 4 TMEM lane quarters
         const int j = dw >> 2;                                  // 0..3
-        const int h = j >> 1, chalf = j & 1;
+        const int chalf = j & 1;
         const int quarter = warp & 3;                           // TMEM lanes this warp may access
-        const int rloc = h * 128 + quarter * 32 + lane;         // row inside the CTA tile
-        const int row = m0 + rloc;
         const bool done = mbar_wait(accum, 0);
         if (!done) atomicOr(p.status, kStatusPipeTimeout);
         tc_fence_after();
-        float v[64];
-        const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN + chalf * 64);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            float part[32];
-            tc_ld32(tbase + c * 32, part);
-            tc_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[c * 32 + i] = part[i];
-        }
-        // FWHT stages h = 1..32 stay inside a 64-column half
-#pragma unroll
-        for (int hs = 1; hs < 64; hs <<= 1) {
-#pragma unroll
-            for (int b = 0; b < 32; ++b) {
-                const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
-                const float a0 = v[i0], a1 = v[i1];
-                v[i0] = a0 + a1;
-                v[i1] = a0 - a1;
-            }
-        }
-        // stage h = 64 pairs column c with c + 64: exchange halves through shared memory (the
-        // operand stages are free once every MMA has completed); rows padded to 129 floats
-        float* xbuf = reinterpret_cast<float*>(smem);
+        float* xbuf = reinterpret_cast<float*>(smem);           // operand stages are free once the MMAs completed
         constexpr int kRow = 129;
+#pragma unroll 1
+        for (int pass = 0; pass < TL::NH / 2; ++pass) {
+            const int h = 2 * pass + (j >> 1);
+            const int rpass = (j >> 1) * 128 + quarter * 32 + lane;     // row inside this pass's 256
+            const int row = m0 + h * 128 + quarter * 32 + lane;
+            float v[64];
+            const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN + chalf * 64);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) xbuf[rloc * kRow + chalf * 64 + i] = v[i];
-        named_bar_sync(1, 32 * kGemmDecWarps);
+            for (int c = 0; c < 2; ++c) {
+                float part[32];
+                tc_ld32(tbase + c * 32, part);
+                tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            const float other = xbuf[rloc * kRow + (chalf ^ 1) * 64 + i];
-            v[i] = chalf == 0 ? v[i] + other : other - v[i];
-        }
-        if (done && row < p.M) {
-            const __half* sv = p.svh + (size_t)nb * kGemmBN + chalf * 64;
-            const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN + chalf * 64;
-            if (p.out_dtype == EXL3_F16) store_row64(static_cast<__half*>(p.y) + off, v, sv);
-            else if (p.out_dtype == EXL3_BF16) store_row64(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
-            else store_row64(static_cast<float*>(p.y) + off, v, sv);
+                for (int i = 0; i < 32; ++i) v[c * 32 + i] = part[i];
+            }
+            // FWHT stages h = 1..32 stay inside a 64-column half
+#pragma unroll
+            for (int hs = 1; hs < 64; hs <<= 1) {
+#pragma unroll
+                for (int b = 0; b < 32; ++b) {
+                    const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
+                    const float a0 = v[i0], a1 = v[i1];
+                    v[i0] = a0 + a1;
+                    v[i1] = a0 - a1;
+                }
+            }
+            // stage h = 64 pairs column c with c + 64: exchange halves through shared memory, rows
+            // padded to 129 floats
+            if (pass > 0) named_bar_sync(1, 32 * kGemmDecWarps);     // the previous pass's reads are done
+#pragma unroll
+            for (int i = 0; i < 64; ++i) xbuf[rpass * kRow + chalf * 64 + i] = v[i];
+            named_bar_sync(1, 32 * kGemmDecWarps);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                const float other = xbuf[rpass * kRow + (chalf ^ 1) * 64 + i];
+                v[i] = chalf == 0 ? v[i] + other : other - v[i];
+            }
+            if (done && row < p.M) {
+                const __half* sv = p.svh + (size_t)nb * kGemmBN + chalf * 64;
+                const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN + chalf * 64;
+                if (p.out_dtype == EXL3_F16) store_row64(static_cast<__half*>(p.y) + off, v, sv);
+                else if (p.out_dtype == EXL3_BF16) store_row64(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
+                else store_row64(static_cast<float*>(p.y) + off, v, sv);
+            }
         }
     }
 
@@ -295,34 +315,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TL::TMEM_COLS));
     }
 }
 
 // ------------------------------------------------------------------------------ host
-template <int K, int CB>
-static int launch_gemm_k(const CUtensorMap& map, const GemmParams& prm, dim3 grid, cudaStream_t s)
+template <int K, int CB, int BM>
+static int launch_gemm_bm(const CUtensorMap& map, const GemmParams& prm, cudaStream_t s)
 {
+    constexpr int SMEM = GemmTile<BM>::SMEM;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemm_kernel<K, CB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(gemm_kernel<K, CB, BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
             return EXL3_E_CUDA;
         attr_set[dev] = true;
     }
-    gemm_kernel<K, CB><<<grid, kGemmThreads, kGemmSmem, s>>>(map, prm);
+    const dim3 grid(prm.n / kGemmBN, (prm.M + BM - 1) / BM);
+    gemm_kernel<K, CB, BM><<<grid, kGemmThreads, SMEM, s>>>(map, prm);
     return launch_status();
 }
 
+// 512-row tiles once a second 256-row tile would be needed (each weight decoded once per 512 rows),
+// as long as they still give about one CTA per SM; else 256-row tiles (more CTAs, each weight decoded
+// once per 256 rows)
+template <int K, int CB>
+static int launch_gemm_k(const CUtensorMap& map, const GemmParams& prm, cudaStream_t s)
+{
+    const long long ctas512 = (long long)(prm.n / kGemmBN) * ((prm.M + 511) / 512);
+    const bool tall = prm.M > 256 && ctas512 * 8 >= (long long)device_sm_count() * 7;
+    return tall ? launch_gemm_bm<K, CB, 512>(map, prm, s) : launch_gemm_bm<K, CB, 256>(map, prm, s);
+}
+
 template <int K>
-static int launch_gemm_cb(int cb, const CUtensorMap& map, const GemmParams& prm, dim3 grid, cudaStream_t s)
+static int launch_gemm_cb(int cb, const CUtensorMap& map, const GemmParams& prm, cudaStream_t s)
 {
     switch (cb) {
-    case 0: return launch_gemm_k<K, 0>(map, prm, grid, s);
-    case 1: return launch_gemm_k<K, 1>(map, prm, grid, s);
-    default: return launch_gemm_k<K, 2>(map, prm, grid, s);
+    case 0: return launch_gemm_k<K, 0>(map, prm, s);
+    case 1: return launch_gemm_k<K, 1>(map, prm, s);
+    default: return launch_gemm_k<K, 2>(map, prm, s);
     }
 }
 
@@ -343,11 +375,12 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
     auto encode = exl3_get_tensormap_encoder();
     if (!encode) return EXL3_E_CUDA;
 
-    // xh: fp16 (M, k) row-major -> 2D map {k, M}, box {64, 256}, 128-byte swizzle, zero fill past M
+    // xh: fp16 (M, k) row-major -> 2D map {k, M}, box {64, 256} (a 512-row tile takes two), 128-byte
+    // swizzle, zero fill past M
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)kGemmBM};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, 256u};
     const cuuint32_t estr[2] = {1, 1};
     if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(xh), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -365,16 +398,15 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
     prm.KT = k / 16;
     prm.NT = n / 16;
     prm.out_dtype = out_dtype;
-    const dim3 grid(n / kGemmBN, (M + kGemmBM - 1) / kGemmBM);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (bits) {
-    case 1: return launch_gemm_cb<1>(codebook, map, prm, grid, s);
-    case 2: return launch_gemm_cb<2>(codebook, map, prm, grid, s);
-    case 3: return launch_gemm_cb<3>(codebook, map, prm, grid, s);
-    case 4: return launch_gemm_cb<4>(codebook, map, prm, grid, s);
-    case 5: return launch_gemm_cb<5>(codebook, map, prm, grid, s);
-    case 6: return launch_gemm_cb<6>(codebook, map, prm, grid, s);
-    case 7: return launch_gemm_cb<7>(codebook, map, prm, grid, s);
-    default: return launch_gemm_cb<8>(codebook, map, prm, grid, s);
+    case 1: return launch_gemm_cb<1>(codebook, map, prm, s);
+    case 2: return launch_gemm_cb<2>(codebook, map, prm, s);
+    case 3: return launch_gemm_cb<3>(codebook, map, prm, s);
+    case 4: return launch_gemm_cb<4>(codebook, map, prm, s);
+    case 5: return launch_gemm_cb<5>(codebook, map, prm, s);
+    case 6: return launch_gemm_cb<6>(codebook, map, prm, s);
+    case 7: return launch_gemm_cb<7>(codebook, map, prm, s);
+    default: return launch_gemm_cb<8>(codebook, map, prm, s);
     }
 }

@@ -12,10 +12,19 @@ import torch
 from .kernels import decode_wt, gemm, had_svh, rot
 
 PREFILL_COL_CHUNK = 16384
-# Up to this many rows (one 256-row tile: every weight decoded once) the fused kernel is used. Above
-# it the fused kernel decodes every weight once per 256 rows, and on B200 at the 27B-class shapes
-# decoding W once to fp16 plus a library GEMM is already as fast at 512 rows and faster beyond.
+# Up to this many rows (one 256-row tile: every weight decoded once) the fused kernel is used. Up to
+# FUSED_WIDE_ROWS it is used too when the output has at least FUSED_WIDE_BLOCKS 128-column blocks: it
+# then runs 512-row tiles (every weight still decoded once) on about one CTA per SM. Beyond that, or
+# for narrower outputs (too few CTAs without a k split), decoding W once to fp16 plus a library GEMM
+# is faster on B200 at the 27B-class shapes (measured: M=512, 5120->17408: fused 793 TFLOP/s against
+# 617; 17408->5120: 414 against 667; M=4096: 892 / 790 against 1086 / 1268).
 FUSED_MAX_ROWS = 256
+FUSED_WIDE_ROWS = 512
+FUSED_WIDE_BLOCKS = 128
+
+
+def use_fused(rows: int, n: int) -> bool:
+    return rows <= FUSED_MAX_ROWS or (rows <= FUSED_WIDE_ROWS and n // 128 >= FUSED_WIDE_BLOCKS)
 
 
 def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, cb: int, suh: torch.Tensor,
@@ -24,7 +33,7 @@ def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, c
     rows = x2.shape[0]
     xh = rot(x2, suh.reshape(1, -1))[0]
     if fused is None:
-        fused = rows <= FUSED_MAX_ROWS
+        fused = use_fused(rows, n)
     if fused and k % 64 == 0 and n % 128 == 0:
         return gemm(xh, tr, k, n, K, cb, svh, out_dtype)
     y = torch.empty((rows, n), dtype=torch.float16, device=x2.device)

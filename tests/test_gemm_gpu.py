@@ -28,9 +28,17 @@ def _case(dev, M, k, n, K, cb, out=torch.float32, seed=0):
     return y.float().cpu().numpy(), ref
 
 
-@pytest.mark.parametrize("M", [1, 7, 100, 256, 257, 600])
+@pytest.mark.parametrize("M", [1, 7, 100, 256, 257, 600, 1100])
 def test_gemm_rows(cuda, M):
     y, ref = _case(cuda, M, 512, 256, 6, 0, seed=M)
+    assert O.max_rel(y, ref) < 2e-3, M
+
+
+@pytest.mark.parametrize("M", [600, 1100])
+def test_gemm_tall_tiles(cuda, M):
+    """Wide enough (148 column blocks) that M > 256 runs 512-row tiles: four accumulators, two TMA
+    boxes per stage, a two-pass epilogue, and a partial last row tile."""
+    y, ref = _case(cuda, M, 256, 148 * 128, 5, 0, seed=M + 3)
     assert O.max_rel(y, ref) < 2e-3, M
 
 
