@@ -81,6 +81,9 @@ typedef struct exl3_gemv_desc {
     int32_t out_dtype;   /* EXL3_F16 or EXL3_BF16 */
     int32_t grid;        /* CTAs to use; 0 = one per SM of the current device */
     int32_t flags;       /* EXL3_GEMV_ROW_EXACT: row r's result does not depend on `rows` */
+    int32_t member_bits[3]; /* bits of each member; 0 = `bits`. Members may differ (a q/k/v group quantised
+                               at different bpw): each then runs on its own share of the CTAs, still one
+                               launch (exl3_gemv, exl3_gemv_qkv_post; not exl3_gemv_peer) */
 } exl3_gemv_desc;
 
 /* exl3_gemv_desc.flags. Without ROW_EXACT a single row takes a CUDA-core path (half2 products,

@@ -32,7 +32,8 @@ _STATUS_EXC = {
 class GemvDesc(ctypes.Structure):
     _fields_ = [("k", ctypes.c_int32), ("n_members", ctypes.c_int32), ("n", ctypes.c_int32 * 3),
                 ("bits", ctypes.c_int32), ("codebook", ctypes.c_int32), ("rows", ctypes.c_int32),
-                ("out_dtype", ctypes.c_int32), ("grid", ctypes.c_int32), ("flags", ctypes.c_int32)]
+                ("out_dtype", ctypes.c_int32), ("grid", ctypes.c_int32), ("flags", ctypes.c_int32),
+                ("member_bits", ctypes.c_int32 * 3)]
 
 
 GEMV_ROW_EXACT = 1

@@ -17,6 +17,8 @@ template int launch_gemv_epi<0>(int, int, const GemvParams&, int, cudaStream_t);
 struct GemvLaunch {
     int grid, J, blocks, KT, gran;
     long long units;
+    bool mixed;                      // members of different bitrates: one CTA segment each
+    int seg_cta[4], seg_bits[3], smem;
 };
 
 // Grid choice. A CTA's time is about its unit count plus a fixed cost per block segment it ends
@@ -86,22 +88,55 @@ static int plan_gemv(const exl3_gemv_desc* d, GemvLaunch* L)
     if (d->bits < 1 || d->bits > 8) return EXL3_E_BITS;
     if (d->codebook < 0 || d->codebook > 2) return EXL3_E_CODEBOOK;
     if (d->out_dtype != EXL3_F16 && d->out_dtype != EXL3_BF16) return EXL3_E_DTYPE;
-    int blocks = 0;
+    int blocks = 0, mb[3] = {d->bits, d->bits, d->bits};
+    L->mixed = false;
     for (int m = 0; m < d->n_members; ++m) {
         if (d->n[m] <= 0 || d->n[m] % 128) return EXL3_E_SHAPE;
         blocks += d->n[m] / 128;
+        mb[m] = d->member_bits[m] ? d->member_bits[m] : d->bits;
+        if (mb[m] < 1 || mb[m] > 8) return EXL3_E_BITS;
+        if (mb[m] != mb[0]) L->mixed = true;
     }
     L->blocks = blocks;
     L->KT = d->k / 16;
     L->units = (long long)blocks * L->KT;
     L->gran = L->KT % kNCW == 0 ? kNCW : 1;
-    const long long granules = L->units / L->gran;
-    long long G = d->grid > 0 ? d->grid : pick_grid(blocks, L->KT, L->gran, device_sm_count());
-    if (G > granules) G = granules;
-    L->grid = (int)G;
-    if ((unsigned long long)L->units * (unsigned long long)(G + 1) >= (1ull << 32)) return EXL3_E_SHAPE;
-    const long long per = (granules + G - 1) / G * L->gran;
-    L->J = (int)((per + L->KT - 1) / L->KT + 1);
+    L->smem = 0;
+    if (!L->mixed) {
+        const long long granules = L->units / L->gran;
+        long long G = d->grid > 0 ? d->grid : pick_grid(blocks, L->KT, L->gran, device_sm_count());
+        if (G > granules) G = granules;
+        L->grid = (int)G;
+        if ((unsigned long long)L->units * (unsigned long long)(G + 1) >= (1ull << 32)) return EXL3_E_SHAPE;
+        const long long per = (granules + G - 1) / G * L->gran;
+        L->J = (int)((per + L->KT - 1) / L->KT + 1);
+        return EXL3_OK;
+    }
+    // Mixed bitrates: each member gets a CTA segment in proportion to its units (the decode costs about
+    // the same per weight at every bitrate), planned inside that share as a launch of its own would be.
+    const int total = d->grid > 0 ? d->grid : device_sm_count();
+    int seg = 0, J = 1;
+    for (int m = 0; m < d->n_members; ++m) {
+        const int bm = d->n[m] / 128;
+        const long long um = (long long)bm * L->KT, gm = um / L->gran;
+        long long cap = (long long)total * um / L->units;
+        cap = cap < 1 ? 1 : cap;
+        long long G = pick_grid(bm, L->KT, L->gran, (int)cap);
+        G = G > gm ? gm : (G < 1 ? 1 : G);
+        if ((unsigned long long)um * (unsigned long long)(G + 1) >= (1ull << 32)) return EXL3_E_SHAPE;
+        const long long per = (gm + G - 1) / G * L->gran;
+        const int Jm = (int)((per + L->KT - 1) / L->KT + 1);
+        J = Jm > J ? Jm : J;
+        L->seg_cta[m] = seg;
+        L->seg_bits[m] = mb[m];
+        seg += (int)G;
+        const int sm = gemv_smem_bytes(mb[m]);
+        L->smem = sm > L->smem ? sm : L->smem;
+    }
+    for (int m = d->n_members; m < 3; ++m) L->seg_bits[m] = mb[0];
+    for (int m = d->n_members; m <= 3; ++m) L->seg_cta[m] = seg;
+    L->grid = seg;
+    L->J = J;
     return EXL3_OK;
 }
 
@@ -179,6 +214,13 @@ static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_
     }
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (L.mixed) {
+        if (peer) return EXL3_E_BITS;                        // row-parallel projections are single linears
+        for (int m = 0; m < 4; ++m) prm.seg_cta[m] = L.seg_cta[m];
+        for (int m = 0; m < 3; ++m) prm.seg_bits[m] = L.seg_bits[m];
+        return post ? launch_gemv_seg<1>(desc->codebook, prm, L.grid, L.smem, s)
+                    : launch_gemv_seg<0>(desc->codebook, prm, L.grid, L.smem, s);
+    }
     if (post) return launch_gemv_epi<1>(desc->bits, desc->codebook, prm, L.grid, s);
     if (peer) return launch_gemv_epi<2>(desc->bits, desc->codebook, prm, L.grid, s);
     return launch_gemv_epi<0>(desc->bits, desc->codebook, prm, L.grid, s);

@@ -54,6 +54,8 @@ struct GemvParams {
     int k, KT, rows, n_total, blocks, out_bf16, J, row_exact, gran;
     long long units;
     exl3_qkv_post_args post; // finish kind 1: members are q, k, v (no y)
+    int seg_cta[4];          // mixed bitrates: member m owns CTAs [seg_cta[m], seg_cta[m + 1])
+    int seg_bits[3];         // mixed bitrates: bits of each member
     int ll_world;            // > 0: rows go as LL words into ll[0..ll_world) (exl3_gemv_peer; no y)
     uint64_t* ll[8];         // inbox (slot, this rank) of every rank of the group
     const uint32_t* epoch;   // own flag block's "last completed" epoch word
@@ -223,23 +225,24 @@ __device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const __half
 // EPI: the finish of a block: 0 = y (exl3_gemv), 1 = exl3_qkv_post's (exl3_gemv_qkv_post), 2 = LL words
 // into the peers' inboxes (exl3_gemv_peer). A template parameter, so the plain GEMV carries no code of
 // the other two (measured: ~2.5 % of the sweep when they shared one kernel).
+// The GEMV of one CTA: CTA c of the G CTAs that share the U granules of units starting at unit ubase
+// (the whole launch, or one member's segment of a mixed-bitrate launch); coff is the launch-wide index
+// of the segment's first CTA (its split-k partials).
 template <int K, int CB, int NCW, bool ROWS1, int EPI>
-__global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
+__device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, const int c, const int G, const int coff,
+                                          const int ubase, const unsigned U)
 {
     using S = GemvShape<K, NCW>;
-    extern __shared__ __align__(128) uint8_t smem[];
     float* red = reinterpret_cast<float*>(smem + S::RING);
     __shared__ int s_last;
 
     const int lane = threadIdx.x & 31;
     const int cw = threadIdx.x >> 5;
     const int ctid = threadIdx.x;
-    const int G = gridDim.x, c = blockIdx.x;
     // CTA ranges are whole granules of p.gran units (16 when k is a multiple of 256), so every block
     // segment inside a CTA is a whole number of rounds of the NCW warps
     const int gran = p.gran;
-    const unsigned U = (unsigned)(p.units / gran);
-    const int u0 = cta_start(c, U, G) * gran, u1 = cta_start(c + 1, U, G) * gran;
+    const int u0 = ubase + cta_start(c, U, G) * gran, u1 = ubase + cta_start(c + 1, U, G) * gran;
     const int n_units = (int)(u1 - u0);
     const int KT = p.KT;
     const int rows = p.rows;
@@ -425,12 +428,12 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
         if (!whole) {
             // one warp publishes the CTA's partial and takes the block's arrival ticket
             if (cw == 0) {
-                float* gp = p.partials + ((size_t)c * p.J + (b - b_first)) * kRedStride;
+                float* gp = p.partials + ((size_t)(coff + c) * p.J + (b - b_first)) * kRedStride;
                 for (int e = lane; e < rows * 128; e += 32) gp[e] = red[e];
                 __syncwarp();                                // the warp's stores, ordered before lane 0's release
                 if (lane == 0) {
-                    const int c_first = owner_cta(b * KT / gran, U, G);
-                    const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
+                    const int c_first = owner_cta((b * KT - ubase) / gran, U, G);
+                    const int c_last = owner_cta(((b + 1) * KT - 1 - ubase) / gran, U, G);
                     // one acquire-release RMW: publishes this CTA's partial and, for the last arriver,
                     // makes every other CTA's partial visible (no separate fences)
                     const unsigned old = atom_add_acq_rel_gpu(&p.counters[b], 1u);
@@ -440,12 +443,13 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             __syncthreads();
             finish = s_last != 0;
             if (finish) {
-                const int c_first = owner_cta(b * KT / gran, U, G);
-                const int c_last = owner_cta(((b + 1) * KT - 1) / gran, U, G);
+                const int c_first = owner_cta((b * KT - ubase) / gran, U, G);
+                const int c_last = owner_cta(((b + 1) * KT - 1 - ubase) / gran, U, G);
+                const float* parts = p.partials + (size_t)coff * p.J * kRedStride;   // the segment's CTAs
                 // CTA c_first holds the block in its slot jj0, every later CTA in its slot 0. Up to 8
                 // partials: one round of loads, added in CTA order; more: part_sums' order. The choice
                 // depends on the grid only, never on `rows`.
-                const int jj0 = b - (int)(cta_start(c_first, U, G) * gran / KT);
+                const int jj0 = b - (ubase + cta_start(c_first, U, G) * gran) / KT;
                 const int E = rows * 128;
                 if (c_last - c_first < 8) {
                     for (int e = ctid; e < E; e += 32 * NCW) {
@@ -453,7 +457,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const int ci = c_first + i;
-                            t[i] = ci <= c_last ? __ldcg(p.partials + ((size_t)ci * p.J + (i == 0 ? jj0 : 0)) * kRedStride + e)
+                            t[i] = ci <= c_last ? __ldcg(parts + ((size_t)ci * p.J + (i == 0 ? jj0 : 0)) * kRedStride + e)
                                                 : 0.f;
                         }
                         float v = t[0];
@@ -464,9 +468,9 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
                     }
                 } else {
                     float* gsum = red + NCW * kRedStride / 2;
-                    if (E <= 128) part_sums<4>(p.partials, p.J, jj0, c_first, c_last, E, ctid, 32 * NCW, gsum);
-                    else if (E <= 256) part_sums<2>(p.partials, p.J, jj0, c_first, c_last, E, ctid, 32 * NCW, gsum);
-                    else part_sums<1>(p.partials, p.J, jj0, c_first, c_last, E, ctid, 32 * NCW, gsum);
+                    if (E <= 128) part_sums<4>(parts, p.J, jj0, c_first, c_last, E, ctid, 32 * NCW, gsum);
+                    else if (E <= 256) part_sums<2>(parts, p.J, jj0, c_first, c_last, E, ctid, 32 * NCW, gsum);
+                    else part_sums<1>(parts, p.J, jj0, c_first, c_last, E, ctid, 32 * NCW, gsum);
                     __syncthreads();
                     for (int e = ctid; e < E; e += 32 * NCW)
                         red[e] = ((gsum[e] + gsum[E + e]) + gsum[2 * E + e]) + gsum[3 * E + e];
@@ -496,6 +500,57 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
             }
         }
         __syncthreads();   // red is reused by the next segment
+    }
+}
+
+template <int K, int CB, int NCW, bool ROWS1, int EPI>
+__global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    gemv_body<K, CB, NCW, ROWS1, EPI>(p, smem, blockIdx.x, gridDim.x, 0, 0, (unsigned)(p.units / p.gran));
+}
+
+// Members of different bitrates in one launch (e.g. q/k/v quantised at different bpw): member m owns
+// the CTAs [seg_cta[m], seg_cta[m + 1]) and runs the body of its own bitrate over its own blocks, so a
+// group still takes one launch (and one fused finish) whatever its members' bitrates.
+template <int CB, int NCW, bool ROWS1, int EPI>
+__global__ void __launch_bounds__(32 * NCW, 1) gemv_seg_kernel(const GemvParams p)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int bx = blockIdx.x;
+    const int m = (p.nm > 2 && bx >= p.seg_cta[2]) ? 2 : ((p.nm > 1 && bx >= p.seg_cta[1]) ? 1 : 0);
+    const int c0 = m == 0 ? 0 : (m == 1 ? p.seg_cta[1] : p.seg_cta[2]);
+    const int c1 = m == 0 ? p.seg_cta[1] : (m == 1 ? p.seg_cta[2] : p.seg_cta[3]);
+    const int b0 = m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]);
+    const int b1 = m + 1 < p.nm ? (m == 0 ? p.blk_off[1] : p.blk_off[2]) : p.blk_off[3];
+    const int bits = m == 0 ? p.seg_bits[0] : (m == 1 ? p.seg_bits[1] : p.seg_bits[2]);
+    const int ubase = b0 * p.KT;
+    const unsigned U = (unsigned)((b1 - b0) * p.KT / p.gran);
+    const int c = bx - c0, G = c1 - c0;
+    switch (bits) {
+    case 1: gemv_body<1, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 2: gemv_body<2, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 3: gemv_body<3, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 4: gemv_body<4, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 5: gemv_body<5, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 6: gemv_body<6, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 7: gemv_body<7, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    default: gemv_body<8, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    }
+}
+
+// Dynamic shared memory of the body for `bits` (a mixed launch takes the largest of its members').
+inline int gemv_smem_bytes(int bits)
+{
+    switch (bits) {
+    case 1: return GemvShape<1, kNCW>::SMEM;
+    case 2: return GemvShape<2, kNCW>::SMEM;
+    case 3: return GemvShape<3, kNCW>::SMEM;
+    case 4: return GemvShape<4, kNCW>::SMEM;
+    case 5: return GemvShape<5, kNCW>::SMEM;
+    case 6: return GemvShape<6, kNCW>::SMEM;
+    case 7: return GemvShape<7, kNCW>::SMEM;
+    default: return GemvShape<8, kNCW>::SMEM;
     }
 }
 
@@ -550,6 +605,39 @@ int launch_gemv_epi(int bits, int cb, const GemvParams& prm, int grid, cudaStrea
     default: return launch_gemv_cb<8, EPI>(cb, prm, grid, s);
     }
 }
+
+template <int CB, bool ROWS1, int EPI>
+static int launch_gemv_seg_v(const GemvParams& prm, int grid, int smem, cudaStream_t s)
+{
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        int mx = 0;
+        for (int b = 1; b <= 8; ++b) mx = gemv_smem_bytes(b) > mx ? gemv_smem_bytes(b) : mx;
+        if (cudaFuncSetAttribute(gemv_seg_kernel<CB, kNCW, ROWS1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 mx) != cudaSuccess)
+            return EXL3_E_CUDA;
+        attr_set[dev] = true;
+    }
+    if (int e_ = launch_pdl(gemv_seg_kernel<CB, kNCW, ROWS1, EPI>, grid, 32 * kNCW, smem, s, prm)) return e_;
+    return launch_status();
+}
+
+// Mixed-bitrate launch for one finish kind (instantiated in exl3_gemv_mixed.cu).
+template <int EPI>
+int launch_gemv_seg(int cb, const GemvParams& prm, int grid, int smem, cudaStream_t s)
+{
+    const bool r1 = prm.rows == 1 && !prm.row_exact;
+    switch (cb) {
+    case 0: return r1 ? launch_gemv_seg_v<0, true, EPI>(prm, grid, smem, s) : launch_gemv_seg_v<0, false, EPI>(prm, grid, smem, s);
+    case 1: return r1 ? launch_gemv_seg_v<1, true, EPI>(prm, grid, smem, s) : launch_gemv_seg_v<1, false, EPI>(prm, grid, smem, s);
+    default: return r1 ? launch_gemv_seg_v<2, true, EPI>(prm, grid, smem, s) : launch_gemv_seg_v<2, false, EPI>(prm, grid, smem, s);
+    }
+}
+
+extern template int launch_gemv_seg<0>(int, const GemvParams&, int, int, cudaStream_t);
+extern template int launch_gemv_seg<1>(int, const GemvParams&, int, int, cudaStream_t);
 
 extern template int launch_gemv_epi<0>(int, int, const GemvParams&, int, cudaStream_t);
 extern template int launch_gemv_epi<1>(int, int, const GemvParams&, int, cudaStream_t);

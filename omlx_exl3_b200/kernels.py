@@ -36,18 +36,23 @@ def _need_cuda(*ts):
 
 class TrellisGemvPlan:
     """y = had128(xh @ W_inner) * svh (out_dtype) for one EXL3 linear or a sibling group of <= 3
-    members sharing K and codebook. xh is (n_members, rows, k): each member's own rotated input.
+    members sharing the codebook. xh is (n_members, rows, k): each member's own rotated input. K is the
+    bitrate, or one per member (members of different bitrates still take one launch: each member runs
+    on its own share of the CTAs; an extension over the reference, whose groups share K).
 
     The plan owns the launch descriptor, an fp16 copy of svh and the scratch (split-k partials and
     per-block arrival counters that every call leaves at zero). One plan must not run on two streams
     at once (the reference plan has the same restriction, kernels.py:284-286)."""
 
-    def __init__(self, k: int, member_ns: list[int], K: int, cb: int, svh: torch.Tensor, rows: int,
+    def __init__(self, k: int, member_ns: list[int], K: int | list[int], cb: int, svh: torch.Tensor, rows: int,
                  out_dtype: torch.dtype = torch.float16, grid: int = 0, row_exact: bool | None = None):
-        assert k % 16 == 0 and all(n % 128 == 0 for n in member_ns) and 1 <= K <= 8 and cb in (0, 1, 2)
+        Ks = [int(x) for x in K] if isinstance(K, (list, tuple)) else [int(K)] * len(member_ns)
+        assert len(Ks) == len(member_ns) and all(1 <= x <= 8 for x in Ks)
+        assert k % 16 == 0 and all(n % 128 == 0 for n in member_ns) and cb in (0, 1, 2)
         assert 1 <= len(member_ns) <= 3 and 1 <= rows <= MAX_GEMV_ROWS
         assert out_dtype in (torch.float16, torch.bfloat16)
-        self.k, self.n, self.K, self.cb, self.rows = k, sum(member_ns), K, cb, rows
+        self.k, self.n, self.K, self.cb, self.rows = k, sum(member_ns), Ks[0], cb, rows
+        self.Ks = Ks
         self.out_dtype = out_dtype
         self.nsub = len(member_ns)
         self.member_ns = list(member_ns)
@@ -57,7 +62,10 @@ class TrellisGemvPlan:
         d.k, d.n_members = k, self.nsub
         for i in range(3):
             d.n[i] = member_ns[i] if i < self.nsub else 0
-        d.bits, d.codebook, d.rows = K, cb, rows
+        d.bits, d.codebook, d.rows = Ks[0], cb, rows
+        mixed = any(x != Ks[0] for x in Ks)
+        for i in range(3):
+            d.member_bits[i] = Ks[i] if mixed and i < self.nsub else 0
         d.out_dtype = dtype_code(out_dtype)
         d.grid = grid
         self.row_exact = ROW_EXACT if row_exact is None else row_exact
@@ -88,10 +96,10 @@ class TrellisGemvPlan:
         if xh.numel() != self.nsub * self.rows * self.k:
             raise ValueError(f"xh has {xh.numel()} elements, expected {self.nsub}x{self.rows}x{self.k}")
         _need_cuda(xh, *trellises)
-        for t, n in zip(trellises, self.member_ns):
-            if t.numel() * t.element_size() != self.k * n * self.K // 8:
+        for t, n, Km in zip(trellises, self.member_ns, self.Ks):
+            if t.numel() * t.element_size() != self.k * n * Km // 8:
                 raise ValueError(f"trellis holds {t.numel() * t.element_size()} bytes, expected "
-                                 f"{self.k * n * self.K // 8} for {self.k}x{n} at {self.K} bpw")
+                                 f"{self.k * n * Km // 8} for {self.k}x{n} at {Km} bpw")
         y = out if out is not None else torch.empty((self.rows, self.n), dtype=self.out_dtype, device=xh.device)
         for i in range(3):
             self._tptr[i] = trellises[i if i < self.nsub else 0].data_ptr()

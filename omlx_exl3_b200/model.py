@@ -22,7 +22,8 @@ import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
-from .kernels import MAX_GEMV_ROWS, add_norm_rot, attn_fits, attn_rot, norm_rot, qkv_post, rot, swiglu_rot
+from .kernels import (MAX_GEMV_ROWS, TrellisGemvPlan, add_norm_rot, attn_fits, attn_rot, norm_rot, qkv_post, rot,
+                      swiglu_rot)
 from .linear import EXL3Linear
 
 
@@ -246,6 +247,40 @@ class _Targets:
         return outs
 
 
+class _MixedQKV:
+    """q, k and v that are not one sibling group (their bitrates differ) but share in_features and the
+    codebook: one GEMV launch with a bitrate per member (TrellisGemvPlan with a list of K), so the decode
+    step still finishes q/k/v with qkv_post's math in that launch."""
+
+    def __init__(self, members: list[EXL3Linear]):
+        for m in members:
+            m._prepare()
+        self.members = members
+        self.k = members[0].in_features
+        self.ns = [m.out_features for m in members]
+        self.Ks = [m._K for m in members]
+        self.cb = members[0]._cb
+        self.rot_suh = torch.cat([m.rot_suh for m in members]).contiguous()     # (3, k)
+        self.svh = torch.cat([m._svh for m in members]).contiguous()
+        self.trs = [m._tr for m in members]
+        self.plans: dict[tuple, TrellisGemvPlan] = {}
+
+    @staticmethod
+    def fits(members: list[EXL3Linear]) -> bool:
+        for m in members:
+            m._prepare()
+        f = members[0]
+        return all(m.in_features == f.in_features and m._cb == f._cb and "bias" not in m and
+                   m.out_features % 128 == 0 for m in members)
+
+    def plan(self, rows: int, out_dtype: torch.dtype) -> TrellisGemvPlan:
+        plan = self.plans.get((rows, out_dtype))
+        if plan is None:
+            plan = self.plans[(rows, out_dtype)] = TrellisGemvPlan(self.k, self.ns, self.Ks, self.cb, self.svh,
+                                                                   rows, out_dtype)
+        return plan
+
+
 class _LayerDecode:
     """Per-layer state of the fused decode step (rows <= MAX_GEMV_ROWS)."""
 
@@ -256,10 +291,15 @@ class _LayerDecode:
         # column slices of each projection inside the unit outputs: (unit index, column offset, width)
         self.qkv_at = [self._locate(self.qkv, lin) for lin in (a.q_proj, a.k_proj, a.v_proj)]
         self.gu_at = [self._locate(self.gate_up, lin) for lin in (m.gate_proj, m.up_proj)]
-        # one q/k/v sibling group in that order: its GEMV can finish with qkv_post as the epilogue
+        # one q/k/v sibling group in that order: its GEMV can finish with qkv_post as the epilogue; q/k/v
+        # of different bitrates become one mixed-bitrate launch with the same finish
         u = self.qkv.units[0]
         self.qkv_group = (u if len(self.qkv.units) == 1 and not isinstance(u, EXL3Linear)
                           and list(u.members) == [a.q_proj, a.k_proj, a.v_proj] else None)
+        qkv = [a.q_proj, a.k_proj, a.v_proj]
+        if self.qkv_group is None and _MixedQKV.fits(qkv):
+            self.qkv_group = _MixedQKV(qkv)
+            self.qkv.suh = self.qkv_group.rot_suh          # the norm writes xh in q, k, v order
 
     @staticmethod
     def _locate(t: _Targets, lin: EXL3Linear) -> tuple[int, int, int]:

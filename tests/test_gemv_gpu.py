@@ -133,6 +133,41 @@ def test_gemv_small_grids_and_many_segments(cuda):
         assert int(plan.counters.abs().sum().item()) == 0
 
 
+def _ref_mixed(trs, k, ns, Ks, cb, xh, svh):
+    outs, o = [], 0
+    for m, (t, n, Km) in enumerate(zip(trs, ns, Ks)):
+        outs.append(O.gemv([t], k, [n], Km, cb, xh[m:m + 1], svh[o:o + n]))
+        o += n
+    return np.concatenate(outs, axis=1)
+
+
+@pytest.mark.parametrize("Ks,ns", [([5, 3, 8], [256, 128, 384]), ([6, 7], [640, 128]), ([8, 5, 5], [1280, 256, 256]),
+                                   ([2, 6, 4], [128, 128, 128])])
+@pytest.mark.parametrize("rows", [1, 2, 8])
+def test_gemv_mixed_bitrates(cuda, Ks, ns, rows):
+    """Members of different bitrates in one launch (each on its own CTA segment) against the oracle of
+    each member, with forced grids too, and the scratch left at rest."""
+    from omlx_exl3_b200.kernels import TrellisGemvPlan
+    rng = np.random.default_rng(sum(Ks) * 10 + rows)
+    k, cb = 1024, 0
+    trs = [O.random_trellis(k, n, Km, 70 + i) for i, (n, Km) in enumerate(zip(ns, Ks))]
+    svh = (rng.standard_normal(sum(ns)) * 0.01).astype(np.float16)
+    xh = rng.standard_normal((len(ns), rows, k)).astype(np.float16)
+    ref = _ref_mixed(trs, k, ns, Ks, cb, xh, svh)
+    for grid in (0, 5, 40):
+        for dt in (torch.float16, torch.bfloat16):
+            plan = TrellisGemvPlan(k, ns, Ks, cb, torch.from_numpy(svh).to(cuda), rows, dt, grid=grid)
+            y = plan(torch.from_numpy(xh).to(cuda), [_t(t, cuda) for t in trs])
+            torch.cuda.synchronize()
+            assert tuple(y.shape) == (rows, sum(ns))
+            assert O.max_rel(y.float().cpu().numpy(), ref) < TOL[dt], (grid, dt)
+            assert int(plan.counters.abs().sum().item()) == 0
+    # every member's result equals its own single-member launch within tolerance, deterministic
+    plan = TrellisGemvPlan(k, ns, Ks, cb, torch.from_numpy(svh).to(cuda), rows, torch.float16)
+    args = (torch.from_numpy(xh).to(cuda), [_t(t, cuda) for t in trs])
+    assert torch.equal(plan(*args), plan(*args))
+
+
 def test_gemv_rejects_bad_input(cuda):
     from omlx_exl3_b200.kernels import TrellisGemvPlan
     svh = torch.ones(256, dtype=torch.float16, device=cuda)

@@ -112,17 +112,20 @@ def test_add_norm_rot_rejects_alias(cuda):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("rows,hq,hkv,K", [(1, 40, 8, 6), (3, 8, 2, 5), (8, 20, 4, 4)])
+@pytest.mark.parametrize("rows,hq,hkv,K", [(1, 40, 8, 6), (3, 8, 2, 5), (8, 20, 4, 4), (1, 40, 8, [6, 5, 8]),
+                                           (2, 5, 1, [7, 6, 5])])
 def test_gemv_qkv_post_epilogue_matches_two_kernels(cuda, dtype, rows, hq, hkv, K):
-    """exl3_gemv_qkv_post == exl3_gemv (y in dtype) followed by exl3_qkv_post, bit for bit."""
+    """exl3_gemv_qkv_post == exl3_gemv (y in dtype) followed by exl3_qkv_post, bit for bit; also with
+    q/k/v at different bitrates (one mixed-bitrate launch)."""
     from omlx_exl3_b200 import kernels
     from omlx_exl3_b200.model import ModelConfig, rope_tables
     k = 1024
     ns = [hq * 128, hkv * 128, hkv * 128]
+    Ks = K if isinstance(K, list) else [K] * 3
     g = torch.Generator(device=cuda)
-    g.manual_seed(rows * 7 + hq + K)
-    trs = [torch.randint(-2 ** 31, 2 ** 31 - 1, (k * n * K // 32,), dtype=torch.int32, device=cuda, generator=g)
-           for n in ns]
+    g.manual_seed(rows * 7 + hq + sum(Ks))
+    trs = [torch.randint(-2 ** 31, 2 ** 31 - 1, (k * n * Km // 32,), dtype=torch.int32, device=cuda, generator=g)
+           for n, Km in zip(ns, Ks)]
     svh = ((torch.randint(0, 2, (sum(ns),), device=cuda, generator=g) * 2 - 1) * 0.03).half()
     xh = torch.randn((3, rows, k), device=cuda, generator=g).half()
     qw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(dtype)
