@@ -226,12 +226,13 @@ class _Targets:
     """The distinct EXL3 consumers (sibling groups or single linears) of one normalised input, with
     their stacked input scales: one rotation kernel writes all their rotated inputs."""
 
-    def __init__(self, linears: list[EXL3Linear]):
-        self.units = []
-        for lin in linears:
-            c = _consumer_of(lin)
-            if all(c is not u for u in self.units):
-                self.units.append(c)
+    def __init__(self, linears: list[EXL3Linear], units: list | None = None):
+        self.units = list(units) if units is not None else []
+        if units is None:
+            for lin in linears:
+                c = _consumer_of(lin)
+                if all(c is not u for u in self.units):
+                    self.units.append(c)
         self.nms = [u.rot_suh.shape[0] for u in self.units]
         self.suh = torch.cat([u.rot_suh for u in self.units]).contiguous()
 
@@ -247,10 +248,10 @@ class _Targets:
         return outs
 
 
-class _MixedQKV:
-    """q, k and v that are not one sibling group (their bitrates differ) but share in_features and the
-    codebook: one GEMV launch with a bitrate per member (TrellisGemvPlan with a list of K), so the decode
-    step still finishes q/k/v with qkv_post's math in that launch."""
+class _MixedGroup:
+    """Linears of one input that are not one sibling group (their bitrates differ) but share in_features
+    and the codebook (q/k/v, gate/up): one GEMV launch with a bitrate per member (TrellisGemvPlan with a
+    list of K); for q/k/v the decode step still finishes with qkv_post's math in that launch."""
 
     def __init__(self, members: list[EXL3Linear]):
         for m in members:
@@ -296,10 +297,23 @@ class _LayerDecode:
         u = self.qkv.units[0]
         self.qkv_group = (u if len(self.qkv.units) == 1 and not isinstance(u, EXL3Linear)
                           and list(u.members) == [a.q_proj, a.k_proj, a.v_proj] else None)
-        qkv = [a.q_proj, a.k_proj, a.v_proj]
-        if self.qkv_group is None and _MixedQKV.fits(qkv):
-            self.qkv_group = _MixedQKV(qkv)
-            self.qkv.suh = self.qkv_group.rot_suh          # the norm writes xh in q, k, v order
+        qkv, gu = [a.q_proj, a.k_proj, a.v_proj], [m.gate_proj, m.up_proj]
+        if self.qkv_group is None and _MixedGroup.fits(qkv):
+            self.qkv_group = _MixedGroup(qkv)
+            self.qkv = _Targets(qkv, units=[self.qkv_group])       # the norm writes xh in q, k, v order
+            self.qkv_at = self._spans(qkv)
+        if len(self.gate_up.units) > 1 and _MixedGroup.fits(gu):
+            self.gate_up = _Targets(gu, units=[_MixedGroup(gu)])
+            self.gu_at = self._spans(gu)
+
+    @staticmethod
+    def _spans(lins: list[EXL3Linear]) -> list[tuple[int, int, int]]:
+        """(unit 0, column offset, width) of each linear inside one mixed group's output."""
+        out, off = [], 0
+        for lin in lins:
+            out.append((0, off, lin.out_features))
+            off += lin.out_features
+        return out
 
     @staticmethod
     def _locate(t: _Targets, lin: EXL3Linear) -> tuple[int, int, int]:

@@ -10,7 +10,8 @@ holds the timed CPU baseline of bench.py (`--impl reference`): the reference dec
 GEMV and the 128-point output rotation.
 
 Generated sources and the library go to oracle/_ref/ only (git-ignored). Needs the reference checkout
-(EXL3_REFERENCE_ROOT, default /root/reference); the GPU box uses the prebuilt library.
+(EXL3_REFERENCE_ROOT, default: the reference checkout's path in the build container); the GPU box
+uses the prebuilt library.
 """
 from __future__ import annotations
 

@@ -29,8 +29,9 @@ MIXED_BITS = {"q_proj": 5, "k_proj": 6, "v_proj": 6, "o_proj": 5, "gate_proj": 6
 @pytest.mark.parametrize("path", ["step", "step_mixed", "modules_fused", "modules_plain"])
 @pytest.mark.parametrize("rows", [1, 3])
 def test_decode_logits_kl(cuda, path, rows):
-    """step: the fused decode step (Qwen3EXL3._forward_decode); step_mixed: the same with q alone and
-    gate/up in separate launches; modules_*: the per-module path with and without the norm/MLP fusions."""
+    """step: the fused decode step (Qwen3EXL3._forward_decode); step_mixed: the same with q/k/v and
+    gate/up at different bitrates (one mixed-bitrate launch each); modules_*: the per-module path with
+    and without the norm/MLP fusions."""
     torch.manual_seed(0)
     model = _small_model(cuda, fuse=path != "modules_plain", bits=MIXED_BITS if path == "step_mixed" else None)
     model.fused_decode = path.startswith("step")
@@ -94,6 +95,17 @@ def test_fused_step_matches_module_path(cuda):
         b = model(toks, cache, pos).float()
     assert torch.allclose(a, b, rtol=2e-2, atol=2e-2)
     assert torch.equal(a.argmax(-1), b.argmax(-1))
+
+
+def test_decode_plan_uses_mixed_bitrate_groups(cuda):
+    """q/k/v and gate/up of different bitrates are each one mixed-bitrate launch in the decode step."""
+    from omlx_exl3_b200.model import _MixedGroup
+    model = _small_model(cuda, bits=MIXED_BITS)
+    assert model._decode_ready()
+    lp = model.__dict__["_decode_plans"][0]
+    assert isinstance(lp.qkv_group, _MixedGroup) and lp.qkv_group.Ks == [5, 6, 6]
+    assert len(lp.gate_up.units) == 1 and isinstance(lp.gate_up.units[0], _MixedGroup)
+    assert lp.gate_up.units[0].Ks == [6, 4] and lp.gu_at == [(0, 0, 2048), (0, 2048, 2048)]
 
 
 def test_sibling_group_and_fusion_installed(cuda):
