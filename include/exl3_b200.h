@@ -208,6 +208,15 @@ EXL3_API int exl3_add_norm_rot(const void* x, const void* d, const void* w, int 
                                const void* suh, int n_members, void* x_out, void* xn, void* xh, void* stream);
 
 /*
+ * Greedy selection: for each of `rows` rows of x (row stride ld elements, dtype EXL3_F16 / EXL3_BF16 /
+ * EXL3_F32), the largest of the first n values (val, as fp32) and its column + index_base (idx); the
+ * first column wins ties, NaN never wins. Replaces: the cast + max reduction of the decode step's greedy
+ * token (the reference samples in oMLX's generate loop).
+ */
+EXL3_API int exl3_argmax(const void* x, int dtype, int rows, int ld, int n, int index_base, float* val,
+                         long long* idx, void* stream);
+
+/*
  * Decode attention fused with o_proj's input rotation, for rows new tokens (head_dim 128, GQA,
  * rows * hq / hkv <= 16) over an fp16 KV cache:
  *   xh[r, h*128 : h*128+128] = fp16( had128( fp16(softmax(q k^T / sqrt(128)) v) * suh[h*128 ..] ) / sqrt(128) )

@@ -87,6 +87,7 @@ SIGNATURES = {
     "exl3_attn_workspace": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_size_t)]),
     "exl3_attn_decode_rot": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "exl3_peer_put": (_I, [ctypes.POINTER(PeerGroupDesc), _I, _P, _I, _I, _P]),
+    "exl3_argmax": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "exl3_gemv_peer": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P, ctypes.POINTER(PeerGroupDesc), _I, _P]),
 }
 

@@ -290,6 +290,20 @@ def attn_rot(q16: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, T:
     return xh
 
 
+def argmax(x: torch.Tensor, n: int | None = None, index_base: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per row of x (rows, ld) fp16/bf16/fp32: (max of the first n values as fp32, its column +
+    index_base as int64); the first column wins ties (exl3_argmax)."""
+    rows, ld = x.shape
+    n = ld if n is None else n
+    _need_cuda(x)
+    assert x.stride(1) == 1 and 1 <= n <= ld
+    val = torch.empty(rows, dtype=torch.float32, device=x.device)
+    idx = torch.empty(rows, dtype=torch.int64, device=x.device)
+    check(lib().exl3_argmax(x.data_ptr(), dtype_code(x.dtype), rows, x.stride(0), n, index_base, val.data_ptr(),
+                            idx.data_ptr(), stream_ptr(x.device)), "exl3_argmax")
+    return val, idx
+
+
 def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float, suh: torch.Tensor,
                  want_xn: bool = True) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
     """h = x + d, RMSNorm(h) * w (MLX rounding) and its rotations: returns (h, xn, xh (NM, rows, K) fp16);

@@ -22,8 +22,8 @@ import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
-from .kernels import (MAX_GEMV_ROWS, TrellisGemvPlan, add_norm_rot, attn_fits, attn_rot, norm_rot, qkv_post, rot,
-                      swiglu_rot)
+from .kernels import (MAX_GEMV_ROWS, TrellisGemvPlan, add_norm_rot, argmax, attn_fits, attn_rot, norm_rot, qkv_post,
+                      rot, swiglu_rot)
 from .linear import EXL3Linear
 
 
@@ -507,10 +507,10 @@ class Qwen3EXL3(nn.Module):
         """Global argmax token per row from the local logit shard (one small all-gather)."""
         v0 = self.vocab_range[0]
         n_valid = self.vocab_range[1] - v0
-        val, idx = local[:, :n_valid].float().max(dim=-1)
+        val, idx = argmax(local, n_valid, v0)                           # one pass over the fp16/bf16 logits
         if self.tp.size == 1:
             return idx
-        pack = torch.stack([val, (idx + v0).float()], dim=-1)            # (rows, 2)
+        pack = torch.stack([val, idx.float()], dim=-1)                  # (rows, 2)
         parts = [torch.empty_like(pack) for _ in range(self.tp.size)]
         dist.all_gather(parts, pack, group=self.tp.group)
         allp = torch.stack(parts)                                        # (tp, rows, 2)

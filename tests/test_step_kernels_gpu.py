@@ -143,3 +143,23 @@ def test_gemv_qkv_post_epilogue_matches_two_kernels(cuda, dtype, rows, hq, hkv, 
     assert torch.equal(q1, q2)
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
     assert plan.workspace_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,ld,n", [(1, 151936, 151936), (3, 19008, 18992), (8, 1000, 999), (2, 37, 5)])
+def test_argmax_matches_torch(cuda, dtype, rows, ld, n):
+    """exl3_argmax against torch on the first n columns: same maximum and, with ties planted, the first
+    column; index_base is added to the index."""
+    from omlx_exl3_b200 import kernels
+    g = torch.Generator(device=cuda)
+    g.manual_seed(rows * 31 + n)
+    x = (4 * torch.randn((rows, ld), device=cuda, generator=g)).to(dtype)
+    x[:, n:] = 1000.0                                               # never read
+    if n > 10:
+        x[0, 3] = x[0, n - 2] = 900.0                               # a tie: the first wins
+    val, idx = kernels.argmax(x, n, index_base=7)
+    ref_v, ref_i = x[:, :n].float().max(dim=-1)
+    torch.cuda.synchronize()
+    assert torch.equal(val, ref_v)
+    first = torch.stack([(x[r, :n].float() == ref_v[r]).nonzero()[0, 0] for r in range(rows)])
+    assert torch.equal(idx, first + 7)
