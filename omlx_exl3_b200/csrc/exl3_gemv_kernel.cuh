@@ -155,29 +155,25 @@ __device__ __forceinline__ void fwht128_rows(float (&v)[4], int lane)
 }
 
 template <typename OT>
-__device__ __forceinline__ void finish_row(float (&v)[4], int lane, const __half* svh, OT* yrow)
+__device__ __forceinline__ void finish_row(float (&v)[4], int lane, const float (&sv)[4], OT* yrow)
 {
     fwht128_rows(v, lane);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = lane + 32 * i;
-        yrow[c] = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
-    }
+    for (int i = 0; i < 4; ++i) yrow[lane + 32 * i] = from_f32<OT>(v[i] * kHadScale * sv[i]);
 }
 
 // Peer finish (exl3_gemv_peer): the row's values rounded to OT exactly as a stored y would be, pushed
 // as LL words (column pairs + the next all-reduce's epoch) into every rank's inbox. Even lanes pair
 // their column with the odd neighbour's.
 template <typename OT>
-__device__ __forceinline__ void finish_row_peer(float (&v)[4], int lane, const __half* svh, const GemvParams& p, int b,
-                                                int r)
+__device__ __forceinline__ void finish_row_peer(float (&v)[4], int lane, const float (&sv)[4], uint32_t e,
+                                                const GemvParams& p, int b, int r)
 {
     fwht128_rows(v, lane);
-    const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(p.epoch) + 1u;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int c = lane + 32 * i;
-        const OT o = from_f32<OT>(v[i] * kHadScale * __half2float(svh[c]));
+        const OT o = from_f32<OT>(v[i] * kHadScale * sv[i]);
         const uint32_t lo = *reinterpret_cast<const unsigned short*>(&o);
         const uint32_t hi = __shfl_down_sync(0xffffffffu, lo, 1);
         if (!(lane & 1)) {
@@ -194,12 +190,12 @@ __device__ __forceinline__ void finish_row_peer(float (&v)[4], int lane, const _
 // the per-head RMSNorm (MLX rounding) and rotate-half RoPE and go to q_out / the k cache, v to the v
 // cache, all at this row's position.
 template <typename T>
-__device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const __half* svh, const GemvParams& p, int b,
+__device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const float (&sv)[4], const GemvParams& p, int b,
                                            int r)
 {
     fwht128_rows(v, lane);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = to_f32(from_f32<T>(v[i] * kHadScale * __half2float(svh[lane + 32 * i])));
+    for (int i = 0; i < 4; ++i) v[i] = to_f32(from_f32<T>(v[i] * kHadScale * sv[i]));
     const exl3_qkv_post_args& a = p.post;
     const int m = b >= p.blk_off[2] ? 2 : (b >= p.blk_off[1] ? 1 : 0);
     const int head = b - (m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]));
@@ -233,6 +229,7 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
                                           const int ubase, const unsigned U)
 {
     using S = GemvShape<K, NCW>;
+    static_assert(NCW >= 8, "the finish gives each of the up to 8 rows its own warp");
     float* red = reinterpret_cast<float*>(smem + S::RING);
     __shared__ int s_last;
 
@@ -414,6 +411,17 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
                 }
             }
         }
+        // The finish's output scales (and the peer push's epoch) are read now, so their round trip
+        // overlaps the reduction and the cross-CTA arrival instead of following them. Warp cw finishes
+        // row cw (rows <= 8 < NCW); the epoch is final here, since the all-reduce that advances it runs
+        // after this kernel has completed.
+        float sv[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t epoch = 0;
+        if (cw < rows) {
+#pragma unroll
+            for (int ii = 0; ii < 4; ++ii) sv[ii] = __half2float(p.svh[(size_t)b * 128 + lane + 32 * ii]);
+            if constexpr (EPI == 2) epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch) + 1u;
+        }
         __syncthreads();
         for (int e = ctid; e < rows * 128; e += 32 * NCW) {
             float v = red[e];
@@ -480,18 +488,18 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
             }
         }
         if (finish) {
-            for (int r = cw; r < rows; r += NCW) {
+            if (cw < rows) {
+                const int r = cw;
                 float v[4];
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) v[ii] = red[r * 128 + lane + 32 * ii];
-                const __half* sv = p.svh + (size_t)b * 128;
                 const size_t yoff = (size_t)r * p.n_total + (size_t)b * 128;
                 if constexpr (EPI == 1) {
                     if (p.out_bf16) finish_qkv<__nv_bfloat16>(v, lane, sv, p, b, r);
                     else finish_qkv<__half>(v, lane, sv, p, b, r);
                 } else if constexpr (EPI == 2) {
-                    if (p.out_bf16) finish_row_peer<__nv_bfloat16>(v, lane, sv, p, b, r);
-                    else finish_row_peer<__half>(v, lane, sv, p, b, r);
+                    if (p.out_bf16) finish_row_peer<__nv_bfloat16>(v, lane, sv, epoch, p, b, r);
+                    else finish_row_peer<__half>(v, lane, sv, epoch, p, b, r);
                 } else if (p.out_bf16) {
                     finish_row(v, lane, sv, reinterpret_cast<__nv_bfloat16*>(p.y) + yoff);
                 } else {
