@@ -126,7 +126,15 @@ def dtype_code(dt: torch.dtype) -> int:
     raise TypeError(f"unsupported dtype {dt}")
 
 
-def stream_ptr(device: torch.device | None = None) -> int:
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def stream_ptr(device: torch.device | int | None = None) -> int:
+    """The current CUDA stream of `device` as a raw cudaStream_t. Every launch asks for it, so the
+    raw accessor is used where torch has it (torch.cuda.current_stream builds a Stream object)."""
+    if _raw_stream is not None:
+        idx = device.index if isinstance(device, torch.device) else device
+        return _raw_stream(torch.cuda.current_device() if idx is None else idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 

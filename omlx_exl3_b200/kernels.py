@@ -82,6 +82,9 @@ class TrellisGemvPlan:
             self.partials = torch.empty(max(pb.value // 4, 4), dtype=torch.float32, device=self.device)
             self.counters = torch.zeros(max(cbytes.value // 4, 1), dtype=torch.int32, device=self.device)
         self._tptr = (ctypes.c_void_p * 3)()
+        # argument objects of every launch, built once
+        self._desc_ref = ctypes.byref(self.desc)
+        self._tptr_arg = ctypes.cast(self._tptr, ctypes.c_void_p)
 
     def workspace_status(self) -> int:
         """The kernel's error word (0 = no bounded wait ever gave up)."""
@@ -103,7 +106,7 @@ class TrellisGemvPlan:
         y = out if out is not None else torch.empty((self.rows, self.n), dtype=self.out_dtype, device=xh.device)
         for i in range(3):
             self._tptr[i] = trellises[i if i < self.nsub else 0].data_ptr()
-        check(lib().exl3_gemv(ctypes.byref(self.desc), xh.data_ptr(), ctypes.cast(self._tptr, ctypes.c_void_p),
+        check(lib().exl3_gemv(self._desc_ref, xh.data_ptr(), self._tptr_arg,
                               self.svh.data_ptr(), y.data_ptr(), self.partials.data_ptr(), self.counters.data_ptr(),
                               stream_ptr(xh.device)), "exl3_gemv")
         return y
@@ -131,7 +134,7 @@ class TrellisGemvPlan:
         a.hq, a.hkv, a.max_len, a.eps = hq, hkv, k_cache.shape[1], float(eps)
         for i in range(3):
             self._tptr[i] = trellises[i].data_ptr()
-        check(lib().exl3_gemv_qkv_post(ctypes.byref(self.desc), xh.data_ptr(), ctypes.cast(self._tptr, ctypes.c_void_p),
+        check(lib().exl3_gemv_qkv_post(self._desc_ref, xh.data_ptr(), self._tptr_arg,
                                        self.svh.data_ptr(), self.partials.data_ptr(), self.counters.data_ptr(),
                                        ctypes.byref(a), stream_ptr(xh.device)), "exl3_gemv_qkv_post")
         return q_out
@@ -146,7 +149,7 @@ class TrellisGemvPlan:
         _need_cuda(xh, *trellises)
         for i in range(3):
             self._tptr[i] = trellises[i if i < self.nsub else 0].data_ptr()
-        check(lib().exl3_gemv_peer(ctypes.byref(self.desc), xh.data_ptr(), ctypes.cast(self._tptr, ctypes.c_void_p),
+        check(lib().exl3_gemv_peer(self._desc_ref, xh.data_ptr(), self._tptr_arg,
                                    self.svh.data_ptr(), self.partials.data_ptr(), self.counters.data_ptr(),
                                    ctypes.byref(peers.desc), slot, stream_ptr(xh.device)), "exl3_gemv_peer")
 
