@@ -298,9 +298,10 @@ def run_ours(args, rank, world, local_rank):
         "gemv_GBps_by_rows": per_rows,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4),
-                     # per average launch: algorithmic bytes x the DRAM/algorithmic ratio 1.0004 of the
-                     # ncu capture in profiles/gemv_kernel_sweep.md (5120->17408, K=6, rows=1)
-                     "traffic": round(float(launch_bytes.mean()) * 1.0004),
+                     # per average launch: algorithmic bytes x the DRAM (read + write) / algorithmic
+                     # ratio 1.0057 of the ncu capture in profiles/gemv_kernel_sweep.md
+                     # (5120->17408, K=6, rows=1)
+                     "traffic": round(float(launch_bytes.mean()) * 1.0057),
                      "traffic_unit": "bytes per launch",
                      "kernel": "exl3::gemv_kernel", "peak_kind": peak_kind,
                      "frac_of_8TBps_nominal": round(achieved / 8000.0, 4)},
