@@ -4,12 +4,14 @@
  * One shared library, libexl3b200.so, built from omlx_exl3_b200/csrc/. Plain pointers and sizes, no
  * framework types: device buffers are owned by the caller, `stream` is a cudaStream_t passed as void*,
  * and every entry point returns 0 (EXL3_OK) or a negative EXL3_E* status (exl3_strerror() names it).
- * No entry point allocates device memory; scratch space is passed in by the caller.
+ * Compute entry points allocate no device memory: scratch space is passed in by the caller (or, for
+ * exl3_gemv_noalloc, lives in a fixed array inside the library). The one allocating entry point is
+ * exl3_peer_create, which makes the tensor-parallel peer buffer.
  *
  * The reference (daig/omlx-exl3) has no C ABI: its kernels are Metal source JIT-compiled through MLX
  * (src/omlx/exl3/kernels.py). Each entry point below names the reference function it replaces. The
- * reference-side Python binding a maintainer would write is shown in INTEGRATION.md; the package
- * omlx_exl3_b200 binds this header through ctypes the same way.
+ * package omlx_exl3_b200 binds this header through ctypes (omlx_exl3_b200/_lib.py), the way a
+ * reference-side Python binding would.
  *
  * Dtype codes: EXL3_F16 = 0, EXL3_BF16 = 1, EXL3_F32 = 2.
  * Trellis buffers are the checkpoint's int16 [k/16][n/16][16K] tensors viewed as uint32 words and
@@ -80,16 +82,15 @@ typedef struct exl3_gemv_desc {
     int32_t rows;        /* 1..8 */
     int32_t out_dtype;   /* EXL3_F16 or EXL3_BF16 */
     int32_t grid;        /* CTAs to use; 0 = one per SM of the current device */
-    int32_t flags;       /* EXL3_GEMV_ROW_EXACT: row r's result does not depend on `rows` */
+    int32_t flags;       /* reserved, 0 (EXL3_GEMV_ROW_EXACT is accepted: every call is row-exact) */
     int32_t member_bits[3]; /* bits of each member; 0 = `bits`. Members may differ (a q/k/v group quantised
                                at different bpw): each then runs on its own share of the CTAs, still one
                                launch (exl3_gemv, exl3_gemv_qkv_post; not exl3_gemv_peer) */
 } exl3_gemv_desc;
 
-/* exl3_gemv_desc.flags. Without ROW_EXACT a single row takes a CUDA-core path (half2 products,
- * fp32 sums every 16 products) that is faster than the tensor-core path used for 2..8 rows; with it,
- * one row also takes the tensor-core path, so row r of any call gives the same bits
- * (the reference kernel's row-exact property, src/omlx/exl3/kernels.py:13-15). */
+/* exl3_gemv_desc.flags. Every row count multiplies exact fp16 products into fp32 accumulators on the
+ * tensor cores, so row r of any call gives the same bits whatever `rows` is (the reference kernel's
+ * row-exact property, src/omlx/exl3/kernels.py:13-15). The flag is kept for callers that set it. */
 enum { EXL3_GEMV_ROW_EXACT = 1 };
 
 /*
@@ -97,9 +98,10 @@ enum { EXL3_GEMV_ROW_EXACT = 1 };
  * that cannot allocate device memory (code running during CUDA graph capture, hosts whose pool
  * allocator owns all device memory, bindings that only receive input/output pointers). The split-k
  * scratch lives in one fixed 4 MiB array inside this library (per device, held until exit), so a
- * call whose scratch would not fit (more than 4095 column blocks of 128, or more than 4 MiB - 16 KiB
+ * call whose scratch would not fit (more than 4096 column blocks of 128, or more than 4 MiB - 16 KiB
  * of partials, e.g. a very wide output on a large grid) returns EXL3_E_WORKSPACE. The first call on
- * each device looks the array's device address up; make that first call before any stream capture.
+ * each device (and the first after that device's context was reset) looks the array's device address
+ * up; make that first call before any stream capture.
  * Every call clears the counters it uses (one memset on `stream`). All calls on one device share the
  * array, so calls that overlap on that GPU (e.g. on two streams) race and corrupt each other's
  * results: issue them one after another on one stream. Each device has its own copy of the array.
@@ -210,7 +212,7 @@ EXL3_API int exl3_add_norm_rot(const void* x, const void* d, const void* w, int 
 /*
  * Greedy selection: for each of `rows` rows of x (row stride ld elements, dtype EXL3_F16 / EXL3_BF16 /
  * EXL3_F32), the largest of the first n values (val, as fp32) and its column + index_base (idx); the
- * first column wins ties, NaN never wins. Replaces: the cast + max reduction of the decode step's greedy
+ * first column wins ties and a NaN counts as the largest value, as in torch.argmax. Replaces: the cast + max reduction of the decode step's greedy
  * token (the reference samples in oMLX's generate loop).
  */
 EXL3_API int exl3_argmax(const void* x, int dtype, int rows, int ld, int n, int index_base, float* val,
@@ -218,7 +220,9 @@ EXL3_API int exl3_argmax(const void* x, int dtype, int rows, int ld, int n, int 
 
 /*
  * Decode attention fused with o_proj's input rotation, for rows new tokens (head_dim 128, GQA,
- * rows * hq / hkv <= 16) over an fp16 KV cache:
+ * rows * hq / hkv <= 64: every speculative-verify width up to 8 rows at 8 heads per kv head) over an
+ * fp16 KV cache. Row r's result does not depend on `rows` (bitwise equal to a one-row call at its
+ * position):
  *   xh[r, h*128 : h*128+128] = fp16( had128( fp16(softmax(q k^T / sqrt(128)) v) * suh[h*128 ..] ) / sqrt(128) )
  * q: fp16 (rows, hq, 128); k_cache, v_cache: fp16 (hkv, max_len, 128), positions [0, T) valid, new
  * row i at position T - rows + i sees positions <= that; suh: fp16 (hq * 128); xh: fp16 (rows, hq * 128).

@@ -1,5 +1,6 @@
 // Greedy token selection of the decode step: per row, the largest of the first n logits and its index
-// (the first one on ties), read straight from the head GEMV's fp16 / bf16 / fp32 output.
+// (the first one on ties), read straight from the head GEMV's fp16 / bf16 / fp32 output. The order is
+// torch.argmax's: a NaN counts as larger than every number, so the first NaN of a row wins.
 //
 // Replaces the framework's cast-to-fp32 + max-reduction pair at the end of the decode step (the
 // reference samples in oMLX's generate loop; this is this package's greedy step). One thread-block
@@ -22,8 +23,10 @@ constexpr int kArgCluster = 8;
 
 __device__ __forceinline__ void arg_better(float& bv, int& bi, float v, int i)
 {
-    // larger value wins; equal values: smaller index; NaN never wins
-    if (v > bv || (v == bv && i < bi)) {
+    // larger value wins, NaN above all numbers; equal values (or two NaNs): the smaller index
+    const bool vn = v != v, bn = bv != bv;
+    const bool take = vn ? (!bn || i < bi) : (!bn && (v > bv || (v == bv && i < bi)));
+    if (take) {
         bv = v;
         bi = i;
     }
@@ -80,7 +83,6 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict
             asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(oi) : "r"(ai) : "memory");
             arg_better(bv, bi, __uint_as_float(ov), (int)oi);
         }
-        if (bi == 0x7fffffff) bi = 0;                // every logit NaN: index 0
         val[r] = bv;
         idx[r] = (long long)bi + index_base;
     }

@@ -148,7 +148,7 @@ extern "C" int exl3_gemv_workspace(const exl3_gemv_desc* desc, size_t* partial_b
     GemvLaunch L;
     if (int e = plan_gemv(desc, &L)) return e;
     if (partial_bytes) *partial_bytes = (size_t)L.grid * L.J * kRedStride * sizeof(float);
-    if (counter_bytes) *counter_bytes = (size_t)(L.blocks + 1) * sizeof(uint32_t);
+    if (counter_bytes) *counter_bytes = (size_t)L.blocks * sizeof(uint32_t);
     return EXL3_OK;
 }
 
@@ -200,7 +200,6 @@ static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_
     prm.blocks = L.blocks;
     prm.out_bf16 = desc->out_dtype == EXL3_BF16;
     prm.J = L.J;
-    prm.row_exact = (desc->flags & EXL3_GEMV_ROW_EXACT) != 0;
     prm.units = L.units;
     prm.gran = L.gran;
     if (post) prm.post = *post;
@@ -239,22 +238,44 @@ namespace exl3 {
 
 // Scratch of the allocation-free entry point: arrival counters first, then split-k partials.
 constexpr size_t kNoAllocScratchBytes = 4u << 20;                 // 4 MiB per device
-constexpr size_t kNoAllocCounterBytes = 16u << 10;                // up to 4095 blocks + status word
+constexpr size_t kNoAllocCounterBytes = 16u << 10;                // arrival counters of up to 4096 blocks
 static __device__ __align__(256) uint8_t g_gemv_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_gemv_noalloc_scratch for the current device, looked up once per device. In host
-// code the array's name is only a host-side stand-in, so the address must come from the runtime.
+// Device address of g_gemv_noalloc_scratch for the current device. In host code the array's name is
+// only a host-side stand-in, so the address comes from the runtime: looked up on the first call on a
+// device, and again whenever that device's current context is a different one (after a
+// cudaDeviceReset the module is loaded afresh and the old address is stale). The context is read
+// through the driver's cuCtxGetCurrent, fetched from the runtime so the library needs no libcuda link.
+static void* current_context()
+{
+    using CtxGetCurrent = int (*)(void**);
+    static CtxGetCurrent fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<CtxGetCurrent>(f);
+    }();
+    void* ctx = nullptr;
+    if (fn && fn(&ctx) != 0) ctx = nullptr;
+    return ctx;
+}
+
 static int noalloc_scratch(void** out)
 {
     static std::mutex mu;
     static void* addr[64] = {nullptr};
+    static const void* ctx_of[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return EXL3_E_CUDA;
+    const void* ctx = current_context();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx != ctx_of[dev]) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch) != cudaSuccess || !p) return EXL3_E_CUDA;
         addr[dev] = p;
+        ctx_of[dev] = current_context();   // the lookup made the device's context current if none was
     }
     *out = addr[dev];
     return EXL3_OK;
@@ -268,7 +289,7 @@ extern "C" int exl3_gemv_noalloc(const exl3_gemv_desc* desc, const void* xh, con
     using namespace exl3;
     GemvLaunch L;
     if (int e = plan_gemv(desc, &L)) return e;
-    const size_t counter_bytes = (size_t)(L.blocks + 1) * sizeof(uint32_t);
+    const size_t counter_bytes = (size_t)L.blocks * sizeof(uint32_t);
     const size_t partial_bytes = (size_t)L.grid * L.J * kRedStride * sizeof(float);
     if (counter_bytes > kNoAllocCounterBytes || partial_bytes > kNoAllocScratchBytes - kNoAllocCounterBytes)
         return EXL3_E_WORKSPACE;

@@ -13,9 +13,9 @@
 // flight). A warp decodes each of the unit's 8 tiles straight into m16n8k16 A fragments (one lane =
 // 8 consecutive stream positions, exl3_common.cuh) and, for 2..8 rows, issues two MMAs per tile
 // against the rows of xh duplicated across each k pair ("split" operands: the 3inst/mcg weight is
-// the sum of two fp16 halves, so A = (lo, hi) and B = (x, x)); accumulators are fp32 registers.
-// For one row the same split words are multiplied on the CUDA cores instead (half2 FMA against
-// (x, x), flushed to fp32 every few units), which avoids the legacy MMA issue limit.
+// the sum of two fp16 halves, so A = (lo, hi) and B = (x, x)); accumulators are fp32 registers, as
+// the reference's fp32 FMAs (kernels.py:215-218). One row takes the same path, so row r of any call
+// has the same bits whatever `rows` is (the reference's row-exact property, kernels.py:13-15).
 //
 // Reduction, fixed order (bitwise reproducible, row-exact): at the end of each block segment the
 // consumer warps sum their accumulators through shared memory in warp order. A block that lies
@@ -50,8 +50,8 @@ struct GemvParams {
     const __half* svh;       // (n_total)
     void* y;                 // (rows, n_total)
     float* partials;         // grid * J * 8 * 128
-    uint32_t* counters;      // blocks, then one status word
-    int k, KT, rows, n_total, blocks, out_bf16, J, row_exact, gran;
+    uint32_t* counters;      // one arrival counter per 128-column block, zero at rest
+    int k, KT, rows, n_total, blocks, out_bf16, J, gran;
     long long units;
     exl3_qkv_post_args post; // finish kind 1: members are q, k, v (no y)
     int seg_cta[4];          // mixed bitrates: member m owns CTAs [seg_cta[m], seg_cta[m + 1])
@@ -62,9 +62,6 @@ struct GemvParams {
 };
 
 constexpr int kRedStride = 8 * 128;   // floats per warp partial (8 rows x 128 columns)
-// rows == 1: the half2 accumulators take kFlush units (4 products per half each) before they are
-// added into fp32, which bounds the fp16 accumulation to 16 products
-constexpr int kFlush = 4;
 
 template <int K, int NCW>
 struct GemvShape {
@@ -224,7 +221,7 @@ __device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const float 
 // The GEMV of one CTA: CTA c of the G CTAs that share the U granules of units starting at unit ubase
 // (the whole launch, or one member's segment of a mixed-bitrate launch); coff is the launch-wide index
 // of the segment's first CTA (its split-k partials).
-template <int K, int CB, int NCW, bool ROWS1, int EPI>
+template <int K, int CB, int NCW, int EPI>
 __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, const int c, const int G, const int coff,
                                           const int ubase, const unsigned U)
 {
@@ -298,24 +295,18 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
     const int g = lane >> 2, q = lane & 3;
     const LaneWindow<K> lw(lane);
     const HashRegs hr = hash_regs<CB>();
-    const bool xlane = ROWS1 || g < rows;         // this lane carries a row of xh
+    const bool xlane = g < rows;                  // this lane carries a row of xh
 
     for (int b = b_first; b <= b_last; ++b) {
         const int m = (p.nm > 1 && b >= p.blk_off[1]) ? ((p.nm > 2 && b >= p.blk_off[2]) ? 2 : 1) : 0;
-        const __half* xrow = p.xh + ((size_t)m * rows + (ROWS1 ? 0 : g)) * p.k;
+        const __half* xrow = p.xh + ((size_t)m * rows + g) * p.k;
         const int sa = max(u0, b * KT) - u0;
         const int se = min(u1, (b + 1) * KT) - u0;
 
-        // MMA path: acc[j] = the m16n8 accumulator of tile j. rows == 1 path: acc[j][0] / [1] are
-        // columns g / g+8 of tile j in fp32, fed from half2 accumulators hacc every kFlush units.
+        // acc[j]: the m16n8 fp32 accumulator of tile j (rows in the n dimension)
         float acc[8][4];
-        __half2 hacc[8][2];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-            hacc[j][0] = hacc[j][1] = __float2half2_rn(0.f);
-        }
-        int since_flush = 0;
+        for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
         const int kt_base = u0 - b * KT;                     // k-slice of unit index 0 (may be < 0)
         int i = sa + ((cw - sa) % NCW + NCW) % NCW;
@@ -348,67 +339,25 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
                 hashes8<K, CB>(w, h, hr);
 #pragma unroll
                 for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t], hr);
-                if constexpr (ROWS1) {
-                    // columns g (positions 0..3) and g+8 (4..7); k 2q, 2q+1, 2q+8, 2q+9
-                    const __half2 xe0 = *reinterpret_cast<const __half2*>(&be0);
-                    const __half2 xo0 = *reinterpret_cast<const __half2*>(&bo0);
-                    const __half2 xe1 = *reinterpret_cast<const __half2*>(&be1);
-                    const __half2 xo1 = *reinterpret_cast<const __half2*>(&bo1);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[0]), xe0, hacc[j][0]);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[1]), xo0, hacc[j][0]);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[2]), xe1, hacc[j][0]);
-                    hacc[j][0] = __hfma2(*reinterpret_cast<const __half2*>(&a[3]), xo1, hacc[j][0]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[4]), xe0, hacc[j][1]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[5]), xo0, hacc[j][1]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[6]), xe1, hacc[j][1]);
-                    hacc[j][1] = __hfma2(*reinterpret_cast<const __half2*>(&a[7]), xo1, hacc[j][1]);
-                } else {
-                    // even k of the tile: (g,2q) (g+8,2q) (g,2q+8) (g+8,2q+8); odd k: the +1 neighbours
-                    mma16816(acc[j], a[0], a[4], a[2], a[6], be0, be1);
-                    mma16816(acc[j], a[1], a[5], a[3], a[7], bo0, bo1);
-                }
+                // even k of the tile: (g,2q) (g+8,2q) (g,2q+8) (g+8,2q+8); odd k: the +1 neighbours
+                mma16816(acc[j], a[0], a[4], a[2], a[6], be0, be1);
+                mma16816(acc[j], a[1], a[5], a[3], a[7], bo0, bo1);
             }
             __syncwarp();                             // the slot is refilled by the next fetch
-            if constexpr (ROWS1) {
-                if (++since_flush == kFlush) {
-                    since_flush = 0;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-#pragma unroll
-                        for (int cc = 0; cc < 2; ++cc) {
-                            const float2 f = __half22float2(hacc[j][cc]);
-                            acc[j][cc] += f.x + f.y;
-                            hacc[j][cc] = __float2half2_rn(0.f);
-                        }
-                }
-            }
         }
 
         // ---- segment end: warp partials -> shared memory, summed in warp order
         float* rw = red + cw * kRedStride;
-        if constexpr (ROWS1) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const float2 f = __half22float2(hacc[j][cc]);
-                    float v = acc[j][cc] + (f.x + f.y);
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);     // the 4 lanes of column g
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    if (q == 0) rw[16 * j + g + 8 * cc] = v;
-                }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int col = 16 * j + g;
-                if (2 * q < rows) {
-                    rw[(2 * q) * 128 + col] = acc[j][0];
-                    rw[(2 * q) * 128 + col + 8] = acc[j][2];
-                }
-                if (2 * q + 1 < rows) {
-                    rw[(2 * q + 1) * 128 + col] = acc[j][1];
-                    rw[(2 * q + 1) * 128 + col + 8] = acc[j][3];
-                }
+        for (int j = 0; j < 8; ++j) {
+            const int col = 16 * j + g;
+            if (2 * q < rows) {
+                rw[(2 * q) * 128 + col] = acc[j][0];
+                rw[(2 * q) * 128 + col + 8] = acc[j][2];
+            }
+            if (2 * q + 1 < rows) {
+                rw[(2 * q + 1) * 128 + col] = acc[j][1];
+                rw[(2 * q + 1) * 128 + col + 8] = acc[j][3];
             }
         }
         // The finish's output scales (and the peer push's epoch) are read now, so their round trip
@@ -511,17 +460,17 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
     }
 }
 
-template <int K, int CB, int NCW, bool ROWS1, int EPI>
+template <int K, int CB, int NCW, int EPI>
 __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    gemv_body<K, CB, NCW, ROWS1, EPI>(p, smem, blockIdx.x, gridDim.x, 0, 0, (unsigned)(p.units / p.gran));
+    gemv_body<K, CB, NCW, EPI>(p, smem, blockIdx.x, gridDim.x, 0, 0, (unsigned)(p.units / p.gran));
 }
 
 // Members of different bitrates in one launch (e.g. q/k/v quantised at different bpw): member m owns
 // the CTAs [seg_cta[m], seg_cta[m + 1]) and runs the body of its own bitrate over its own blocks, so a
 // group still takes one launch (and one fused finish) whatever its members' bitrates.
-template <int CB, int NCW, bool ROWS1, int EPI>
+template <int CB, int NCW, int EPI>
 __global__ void __launch_bounds__(32 * NCW, 1) gemv_seg_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -536,14 +485,14 @@ __global__ void __launch_bounds__(32 * NCW, 1) gemv_seg_kernel(const GemvParams 
     const unsigned U = (unsigned)((b1 - b0) * p.KT / p.gran);
     const int c = bx - c0, G = c1 - c0;
     switch (bits) {
-    case 1: gemv_body<1, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    case 2: gemv_body<2, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    case 3: gemv_body<3, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    case 4: gemv_body<4, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    case 5: gemv_body<5, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    case 6: gemv_body<6, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    case 7: gemv_body<7, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
-    default: gemv_body<8, CB, NCW, ROWS1, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 1: gemv_body<1, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 2: gemv_body<2, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 3: gemv_body<3, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 4: gemv_body<4, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 5: gemv_body<5, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 6: gemv_body<6, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    case 7: gemv_body<7, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
+    default: gemv_body<8, CB, NCW, EPI>(p, smem, c, G, c0, ubase, U); break;
     }
 }
 
@@ -563,28 +512,21 @@ inline int gemv_smem_bytes(int bits)
 }
 
 
-template <int K, int CB, bool ROWS1, int EPI>
-static int launch_gemv_v(const GemvParams& prm, int grid, cudaStream_t s)
+template <int K, int CB, int EPI>
+static int launch_gemv_k(const GemvParams& prm, int grid, cudaStream_t s)
 {
     using S = GemvShape<K, kNCW>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemv_kernel<K, CB, kNCW, ROWS1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(gemv_kernel<K, CB, kNCW, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  S::SMEM) != cudaSuccess)
             return EXL3_E_CUDA;
         attr_set[dev] = true;
     }
-    if (int e_ = launch_pdl(gemv_kernel<K, CB, kNCW, ROWS1, EPI>, grid, S::THREADS, S::SMEM, s, prm)) return e_;
+    if (int e_ = launch_pdl(gemv_kernel<K, CB, kNCW, EPI>, grid, S::THREADS, S::SMEM, s, prm)) return e_;
     return launch_status();
-}
-
-template <int K, int CB, int EPI>
-static int launch_gemv_k(const GemvParams& prm, int grid, cudaStream_t s)
-{
-    return prm.rows == 1 && !prm.row_exact ? launch_gemv_v<K, CB, true, EPI>(prm, grid, s)
-                                           : launch_gemv_v<K, CB, false, EPI>(prm, grid, s);
 }
 
 template <int K, int EPI>
@@ -614,7 +556,7 @@ int launch_gemv_epi(int bits, int cb, const GemvParams& prm, int grid, cudaStrea
     }
 }
 
-template <int CB, bool ROWS1, int EPI>
+template <int CB, int EPI>
 static int launch_gemv_seg_v(const GemvParams& prm, int grid, int smem, cudaStream_t s)
 {
     static bool attr_set[64] = {false};
@@ -623,12 +565,12 @@ static int launch_gemv_seg_v(const GemvParams& prm, int grid, int smem, cudaStre
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
         int mx = 0;
         for (int b = 1; b <= 8; ++b) mx = gemv_smem_bytes(b) > mx ? gemv_smem_bytes(b) : mx;
-        if (cudaFuncSetAttribute(gemv_seg_kernel<CB, kNCW, ROWS1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(gemv_seg_kernel<CB, kNCW, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  mx) != cudaSuccess)
             return EXL3_E_CUDA;
         attr_set[dev] = true;
     }
-    if (int e_ = launch_pdl(gemv_seg_kernel<CB, kNCW, ROWS1, EPI>, grid, 32 * kNCW, smem, s, prm)) return e_;
+    if (int e_ = launch_pdl(gemv_seg_kernel<CB, kNCW, EPI>, grid, 32 * kNCW, smem, s, prm)) return e_;
     return launch_status();
 }
 
@@ -636,11 +578,10 @@ static int launch_gemv_seg_v(const GemvParams& prm, int grid, int smem, cudaStre
 template <int EPI>
 int launch_gemv_seg(int cb, const GemvParams& prm, int grid, int smem, cudaStream_t s)
 {
-    const bool r1 = prm.rows == 1 && !prm.row_exact;
     switch (cb) {
-    case 0: return r1 ? launch_gemv_seg_v<0, true, EPI>(prm, grid, smem, s) : launch_gemv_seg_v<0, false, EPI>(prm, grid, smem, s);
-    case 1: return r1 ? launch_gemv_seg_v<1, true, EPI>(prm, grid, smem, s) : launch_gemv_seg_v<1, false, EPI>(prm, grid, smem, s);
-    default: return r1 ? launch_gemv_seg_v<2, true, EPI>(prm, grid, smem, s) : launch_gemv_seg_v<2, false, EPI>(prm, grid, smem, s);
+    case 0: return launch_gemv_seg_v<0, EPI>(prm, grid, smem, s);
+    case 1: return launch_gemv_seg_v<1, EPI>(prm, grid, smem, s);
+    default: return launch_gemv_seg_v<2, EPI>(prm, grid, smem, s);
     }
 }
 

@@ -1,19 +1,27 @@
-"""Decode-path fusion of EXL3 input rotations into the kernels that produce their inputs.
+"""Fused input rotations for eager decode: the producer of an EXL3 input writes its rotation too.
 
-Mirrors daig/omlx-exl3 src/omlx/exl3/fusion.py on torch modules. Every EXL3 linear consumes
-xh = had128(x * suh) / sqrt(128). Unfused, a decode step pays a rotation launch per linear or sibling
-group on top of the producer's own kernel. For rows <= MAX_GEMV_ROWS (decode and speculative verify):
+Each EXL3 consumer (a linear, or a sibling group of them) reads xh = H(x * suh), the 128-point
+Walsh-Hadamard rotation of its input. Called module by module, every consumer launches that rotation
+itself after the kernel that produced x. At decode widths (rows <= MAX_GEMV_ROWS) two kinds of producer
+can emit the rotations as a by-product instead:
 
-  RMSNorm -> EXL3 consumers  input_layernorm -> q/k/v, post_attention_layernorm -> gate/up, the final
-                             norm -> lm_head: one kernel (kernels.norm_rot) writes the norm output and
-                             every consumer's rotated input, grouped or not
-  SwiGLU -> down_proj        one kernel (kernels.swiglu_rot) from the gate/up GEMV output to
-                             down_proj's rotated input
+  norm sites   an RMSNorm read only by EXL3 consumers (attention input norm -> q/k/v or
+               in_proj_qkv/z, MLP input norm -> gate/up, final norm -> lm_head): kernels.norm_rot writes
+               the normalised tensor and the rotated input of every consumer in one launch
+  MLP sites    gate/up sibling group -> SwiGLU -> down_proj: kernels.swiglu_rot turns the gate/up GEMV
+               output straight into down_proj's rotated input
 
-Priming is keyed on the identity of the norm's output tensor: a consumer that receives any other
-tensor (a reshape, a cast) computes the rotation itself, so every call path stays correct. Modules
-keep their classes' behaviour for prefill (rows > MAX_GEMV_ROWS); the fused classes are subclasses
-swapped in per instance, so isinstance checks elsewhere still hold.
+`fuse_decode(model)` finds the sites and attaches a `FusionSite` to each producer module. The site
+replaces the module's forward through an instance attribute only, so the module keeps its class,
+parameters and state-dict keys; the site's forward runs the fused kernel at decode widths while
+`ENABLED` is true and the original forward otherwise. The rotations are handed over through the
+consumers' `prime(x, xh)` hook, which a consumer honours only when its next input is the very tensor
+object the norm returned; a consumer reached through anything else (a view, a cast) rotates for
+itself, so a missed hand-over costs a launch, never a wrong result. `unfuse(model)` restores the
+original forwards.
+
+Reference: daig/omlx-exl3 src/omlx/exl3/fusion.py (the same two fusions on MLX modules; `fuse_decode`,
+`ENABLED` and the consumer hooks are the names the oMLX integration calls).
 """
 from __future__ import annotations
 
@@ -23,120 +31,164 @@ from torch import nn
 from .kernels import MAX_GEMV_ROWS, norm_rot, swiglu_rot
 from .linear import EXL3Linear
 
-_fused_classes: dict = {}
-ENABLED = True          # runtime switch (benchmarks): False makes the fused modules behave like their bases
+ENABLED = True          # False sends every fused module down its original forward (for A/B timing)
+
+# (module holding the linears, linear names) whose outputs a decoder layer's input norm feeds
+_ATTENTION_INPUTS = (("self_attn", ("q_proj", "k_proj", "v_proj")), ("linear_attn", ("in_proj_qkv", "in_proj_z")))
 
 
-class _Consumers:
-    """The EXL3 consumers (sibling groups or single linears) of one norm output, primed together."""
-
-    def __init__(self, consumers: list):
-        self.consumers = consumers
-        self.nms = [c.rot_suh.shape[0] for c in consumers]
-        self.rot_suh = torch.cat([c.rot_suh for c in consumers]).contiguous() if len(consumers) > 1 \
-            else consumers[0].rot_suh
-
-    def prime(self, x: torch.Tensor, xh: torch.Tensor):
-        if len(self.consumers) == 1:
-            self.consumers[0].prime(x, xh)
-            return
-        o = 0
-        for c, nm in zip(self.consumers, self.nms):
-            c.prime(x, xh[o:o + nm])
-            o += nm
+def _decode_rows(x: torch.Tensor) -> int:
+    return x.numel() // x.shape[-1]
 
 
-def _norm_eps(norm) -> float:
-    eps = getattr(norm, "eps", None)
-    if eps is None:
-        eps = getattr(norm, "variance_epsilon", None)
-    return float(eps) if eps is not None else float(torch.finfo(norm.weight.dtype).eps)
+class FusionSite:
+    """One producer module whose forward is taken over for decode widths."""
+
+    kind = "site"
+
+    def __init__(self, module: nn.Module):
+        self.module = module
+        self.original = module.forward                 # bound method of the module's class
+
+    def install(self):
+        self.module.forward = self.forward             # instance attribute: shadows the class method
+
+    def uninstall(self):
+        self.module.__dict__.pop("forward", None)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not ENABLED or _decode_rows(x) > MAX_GEMV_ROWS:
+            return self.original(x)
+        return self.fused(x)
+
+    def fused(self, x: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError
 
 
-def _fused_norm_class(base):
-    if ("norm", base) not in _fused_classes:
-        class FusedNorm(base):
-            def forward(self, x):
-                rows = x.numel() // x.shape[-1]
-                if rows > MAX_GEMV_ROWS or not ENABLED:
-                    return base.forward(self, x)
-                target = self.__dict__["_exl3_target"]
-                xn, xh = norm_rot(x.reshape(rows, x.shape[-1]), self.weight, _norm_eps(self), target.rot_suh)
-                xn = xn.reshape(x.shape)
-                target.prime(xn, xh)
-                return xn
+class NormSite(FusionSite):
+    """RMSNorm -> its EXL3 consumers: one norm_rot launch writes xn and every consumer's xh."""
 
-        FusedNorm.__name__ = FusedNorm.__qualname__ = base.__name__
-        _fused_classes[("norm", base)] = FusedNorm
-    return _fused_classes[("norm", base)]
+    kind = "norm"
 
+    def __init__(self, norm: nn.Module, units: list, kind: str = "norm"):
+        super().__init__(norm)
+        self.kind = kind                  # "norm", or "head" for the final norm before the output head
+        self.units = units
+        self.widths = [u.rot_suh.shape[0] for u in units]                  # rotations per unit
+        self.suh = torch.cat([u.rot_suh for u in units]).contiguous()      # (sum(widths), k)
+        self.eps = _eps_of(norm)
 
-def _fused_mlp_class(base):
-    if ("mlp", base) not in _fused_classes:
-        class FusedMLP(base):
-            def forward(self, x):
-                rows = x.numel() // x.shape[-1]
-                if rows > MAX_GEMV_ROWS or not ENABLED:
-                    return base.forward(self, x)
-                gu = self.gate_proj._group.gemv(x, torch.float16)        # (rows, 2 * hidden): [gate | up]
-                xh = swiglu_rot(gu, self.down_proj.rot_suh.reshape(-1))
-                y = self.down_proj.gemv_rotated(xh, x.dtype)
-                return y.reshape(x.shape[:-1] + (y.shape[-1],))
-
-        FusedMLP.__name__ = FusedMLP.__qualname__ = base.__name__
-        _fused_classes[("mlp", base)] = FusedMLP
-    return _fused_classes[("mlp", base)]
+    def fused(self, x: torch.Tensor) -> torch.Tensor:
+        k = x.shape[-1]
+        xn, xh = norm_rot(x.reshape(-1, k), self.module.weight, self.eps, self.suh)
+        xn = xn.view(x.shape)
+        start = 0
+        for unit, width in zip(self.units, self.widths):
+            unit.prime(xn, xh[start:start + width])
+            start += width
+        return xn
 
 
-def _consumers(module, names) -> list | None:
-    """Distinct EXL3 consumers (group, else the linear itself) of the named linears, in order."""
-    out = []
-    for n in names:
-        lin = getattr(module, n, None) if module is not None else None
+class MlpSite(FusionSite):
+    """gate/up group -> SwiGLU -> down_proj: the SwiGLU kernel emits down_proj's rotated input."""
+
+    kind = "mlp"
+
+    def __init__(self, mlp: nn.Module, gate_up, down: EXL3Linear):
+        super().__init__(mlp)
+        self.gate_up, self.down = gate_up, down
+
+    def fused(self, x: torch.Tensor) -> torch.Tensor:
+        gu = self.gate_up.gemv(x, torch.float16)                           # (rows, 2 * n): gate | up
+        xh = swiglu_rot(gu, self.down.rot_suh.reshape(-1))
+        y = self.down.gemv_rotated(xh, x.dtype)
+        return y.view(*x.shape[:-1], y.shape[-1])
+
+
+def _eps_of(norm: nn.Module) -> float:
+    for attr in ("eps", "variance_epsilon"):
+        v = getattr(norm, attr, None)
+        if v is not None:
+            return float(v)
+    return float(torch.finfo(norm.weight.dtype).eps)
+
+
+def _is_rms_norm(m) -> bool:
+    return isinstance(m, nn.RMSNorm) or bool(getattr(m, "_exl3_rms_norm", False))
+
+
+def _units_of(owner: nn.Module | None, names) -> list | None:
+    """The distinct consumers (sibling group, else the linear) behind the named linears of owner, in
+    first-use order; None unless every name is an EXL3Linear."""
+    if owner is None:
+        return None
+    units: list = []
+    for name in names:
+        lin = getattr(owner, name, None)
         if not isinstance(lin, EXL3Linear):
             return None
-        c = lin._group if lin._group is not None else lin
-        if all(c is not o for o in out):
-            out.append(c)
-    return out
+        unit = lin._group or lin
+        if not any(unit is u for u in units):
+            units.append(unit)
+    return units
 
 
-def _is_rms_norm(norm) -> bool:
-    return getattr(norm, "_exl3_rms_norm", False) or type(norm) is nn.RMSNorm
-
-
-def _fuse_norm(norm, consumers) -> bool:
+def _norm_site(norm, units, kind: str = "norm") -> NormSite | None:
     w = getattr(norm, "weight", None)
-    if not consumers or not _is_rms_norm(norm) or w is None or w.shape[0] % 1024 \
-            or w.dtype not in (torch.bfloat16, torch.float16):
-        return False
-    norm.__dict__["_exl3_target"] = _Consumers(consumers)       # plain attribute: not a child module
-    norm.__class__ = _fused_norm_class(type(norm))
-    return True
+    if not units or not _is_rms_norm(norm) or w is None:
+        return None
+    if w.dtype not in (torch.float16, torch.bfloat16) or w.shape[0] % 1024:   # norm_rot's shape rule
+        return None
+    return NormSite(norm, units, kind)
 
 
-def fuse_decode(model: nn.Module) -> dict[str, int]:
-    """Install the decode-path fusions on every eligible decoder layer (and the output head)."""
-    counts = {"norm": 0, "mlp": 0, "head": 0}
+def _mlp_site(mlp) -> MlpSite | None:
+    gate, up, down = (getattr(mlp, n, None) for n in ("gate_proj", "up_proj", "down_proj"))
+    if not all(isinstance(m, EXL3Linear) for m in (gate, up, down)) or "bias" in down:
+        return None
+    group = gate._group
+    if group is None or group.members != [gate, up] or gate.out_features != up.out_features:
+        return None
+    return MlpSite(mlp, group, down)
+
+
+def find_sites(model: nn.Module) -> list[FusionSite]:
+    """Every fusable producer of the model: per decoder layer its two norms and its MLP, then the
+    final norm in front of the output head."""
+    sites: list[FusionSite | None] = []
     for _, layer in model.named_modules():
-        if not all(hasattr(layer, k) for k in ("input_layernorm", "post_attention_layernorm", "mlp")):
+        if not all(hasattr(layer, a) for a in ("input_layernorm", "post_attention_layernorm", "mlp")):
             continue
-        if hasattr(layer, "self_attn"):
-            first = _consumers(layer.self_attn, ("q_proj", "k_proj", "v_proj"))
-        else:
-            first = _consumers(getattr(layer, "linear_attn", None), ("in_proj_qkv", "in_proj_z"))
-        counts["norm"] += _fuse_norm(layer.input_layernorm, first)
-        mlp = layer.mlp
-        second = _consumers(mlp, ("gate_proj", "up_proj"))
-        counts["norm"] += _fuse_norm(layer.post_attention_layernorm, second)
-        gu = mlp.gate_proj._group if second else None
-        if gu is not None and len(gu.members) == 2 and gu.members[0] is mlp.gate_proj \
-                and gu.members[1] is mlp.up_proj and gu.ns[0] == gu.ns[1] \
-                and isinstance(getattr(mlp, "down_proj", None), EXL3Linear) and "bias" not in mlp.down_proj:
-            mlp.__class__ = _fused_mlp_class(type(mlp))
-            counts["mlp"] += 1
+        attn_units = None
+        for owner_name, names in _ATTENTION_INPUTS:
+            owner = getattr(layer, owner_name, None)
+            if owner is not None:
+                attn_units = _units_of(owner, names)
+                break
+        sites.append(_norm_site(layer.input_layernorm, attn_units))
+        sites.append(_norm_site(layer.post_attention_layernorm, _units_of(layer.mlp, ("gate_proj", "up_proj"))))
+        sites.append(_mlp_site(layer.mlp))
     lm = getattr(model, "language_model", model)
     inner = getattr(lm, "model", None)
     if inner is not None and hasattr(inner, "norm"):
-        counts["head"] += _fuse_norm(inner.norm, _consumers(lm, ("lm_head",)))
+        sites.append(_norm_site(inner.norm, _units_of(lm, ("lm_head",)), kind="head"))
+    return [s for s in sites if s is not None]
+
+
+def fuse_decode(model: nn.Module) -> dict[str, int]:
+    """Install the decode-width fusions on every eligible site; returns how many of each kind."""
+    unfuse(model)
+    sites = find_sites(model)
+    for s in sites:
+        s.install()
+    model.__dict__["_exl3_fusion_sites"] = sites
+    counts = {"norm": 0, "mlp": 0, "head": 0}
+    for s in sites:
+        counts[s.kind] += 1
     return counts
+
+
+def unfuse(model: nn.Module) -> None:
+    """Remove the fusions installed by fuse_decode (the modules' own forwards run again)."""
+    for s in model.__dict__.pop("_exl3_fusion_sites", []):
+        s.uninstall()

@@ -15,7 +15,6 @@ to another implementation.
 from __future__ import annotations
 
 import ctypes
-import os
 
 import torch
 
@@ -23,9 +22,6 @@ from . import _lib
 from ._lib import GemvDesc, check, dtype_code, lib, ptr, stream_ptr
 
 MAX_GEMV_ROWS = 8
-# Default for new plans: True makes every GEMV row-exact (one row takes the tensor-core path too, so a
-# speculative-verify row gives the same bits as plain decoding); env OMLX_EXL3_ROW_EXACT=1.
-ROW_EXACT = os.environ.get("OMLX_EXL3_ROW_EXACT") == "1"
 
 
 def _need_cuda(*ts):
@@ -35,17 +31,19 @@ def _need_cuda(*ts):
 
 
 class TrellisGemvPlan:
-    """y = had128(xh @ W_inner) * svh (out_dtype) for one EXL3 linear or a sibling group of <= 3
-    members sharing the codebook. xh is (n_members, rows, k): each member's own rotated input. K is the
-    bitrate, or one per member (members of different bitrates still take one launch: each member runs
-    on its own share of the CTAs; an extension over the reference, whose groups share K).
+    """A reusable launch of the decode GEMV for fixed shapes: 1-3 members (linears read together, one
+    codebook), `rows` input rows, output dtype. A call takes the members' rotated inputs, stacked
+    member-major as xh (n_members, rows, k), and their trellis words, and returns every member's
+    H(xh_m @ W_m) * svh side by side as (rows, sum(member_ns)). K is one bitrate for all members or one
+    per member (members of different bitrates still take one launch, each on its own share of the
+    CTAs; the reference's groups share one K).
 
     The plan owns the launch descriptor, an fp16 copy of svh and the scratch (split-k partials and
     per-block arrival counters that every call leaves at zero). One plan must not run on two streams
     at once (the reference plan has the same restriction, kernels.py:284-286)."""
 
     def __init__(self, k: int, member_ns: list[int], K: int | list[int], cb: int, svh: torch.Tensor, rows: int,
-                 out_dtype: torch.dtype = torch.float16, grid: int = 0, row_exact: bool | None = None):
+                 out_dtype: torch.dtype = torch.float16, grid: int = 0):
         Ks = [int(x) for x in K] if isinstance(K, (list, tuple)) else [int(K)] * len(member_ns)
         assert len(Ks) == len(member_ns) and all(1 <= x <= 8 for x in Ks)
         assert k % 16 == 0 and all(n % 128 == 0 for n in member_ns) and cb in (0, 1, 2)
@@ -68,8 +66,7 @@ class TrellisGemvPlan:
             d.member_bits[i] = Ks[i] if mixed and i < self.nsub else 0
         d.out_dtype = dtype_code(out_dtype)
         d.grid = grid
-        self.row_exact = ROW_EXACT if row_exact is None else row_exact
-        d.flags = _lib.GEMV_ROW_EXACT if self.row_exact else 0
+        d.flags = 0
         self.desc = d
         self.device = svh.device
         _need_cuda(svh)
@@ -85,10 +82,6 @@ class TrellisGemvPlan:
         # argument objects of every launch, built once
         self._desc_ref = ctypes.byref(self.desc)
         self._tptr_arg = ctypes.cast(self._tptr, ctypes.c_void_p)
-
-    def workspace_status(self) -> int:
-        """The kernel's error word (0 = no bounded wait ever gave up)."""
-        return int(self.counters[self.blocks].item())
 
     def __call__(self, xh: torch.Tensor, trellises: list[torch.Tensor], out: torch.Tensor | None = None) -> torch.Tensor:
         """trellises: one flat uint32/int32 view per member. Returns (rows, n) in out_dtype."""
@@ -260,8 +253,9 @@ _ATTN_WS: dict = {}
 
 
 def attn_fits(rows: int, hq: int, hkv: int) -> bool:
-    """Whether attn_rot handles this shape (one m16 tile of q vectors per kv head)."""
-    return hq % hkv == 0 and rows * (hq // hkv) <= 16
+    """Whether attn_rot handles this shape: up to 64 q vectors (rows x heads per kv head), in groups of
+    16 per CTA."""
+    return hq % hkv == 0 and rows * (hq // hkv) <= 64
 
 
 def attn_rot(q16: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, T: int, suh: torch.Tensor,
@@ -328,20 +322,48 @@ def add_norm_rot(x: torch.Tensor, d: torch.Tensor, w: torch.Tensor, eps: float, 
     return h, xn, xh
 
 
+class _StatusWord:
+    """A device's prefill-GEMM status word (the kernel ORs an error bit into it when a bounded wait
+    gives up) and a pinned host mirror of it. After every GEMM launch outside stream capture the word
+    is copied into the mirror asynchronously; each launch first looks at the mirror, so an error raises
+    at a later call without the host ever waiting for the GPU. `read()` is the synchronous check."""
+
+    def __init__(self, device: torch.device):
+        self.device = torch.device(device)
+        self.word = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.mirror = torch.zeros(4, dtype=torch.int32).pin_memory()
+
+    def raise_if_set(self, value: int):
+        if value:
+            raise RuntimeError(f"exl3_gemm on {self.device}: a pipeline wait timed out (status 0x{value:x}); "
+                               "the outputs of the failed call are invalid")
+
+    def before_launch(self):
+        self.raise_if_set(int(self.mirror[0]))
+
+    def after_launch(self):
+        if not torch.cuda.is_current_stream_capturing():
+            self.mirror.copy_(self.word, non_blocking=True)
+
+    def read(self) -> int:
+        return int(self.word[0].item())
+
+
 _status_words: dict = {}
 
 
-def _status(device: torch.device) -> torch.Tensor:
-    t = _status_words.get(device)
-    if t is None:
-        t = _status_words[device] = torch.zeros(4, dtype=torch.int32, device=device)
-    return t
+def _status(device: torch.device) -> _StatusWord:
+    key = torch.device(device)
+    if key not in _status_words:
+        _status_words[key] = _StatusWord(key)
+    return _status_words[key]
 
 
 def gemm(xh: torch.Tensor, trellis_u32: torch.Tensor, k: int, n: int, K: int, cb: int, svh: torch.Tensor,
          out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None) -> torch.Tensor:
     """Prefill product with the trellis decoded in the kernel: out_dtype(had128(xh @ W) / sqrt(128) * svh)
-    for xh fp16 (M, k). Needs k % 64 == 0 and n % 128 == 0 (EXL3Linear._prefill, linear.py:97-105)."""
+    for xh fp16 (M, k). Needs k % 64 == 0 and n % 128 == 0 (EXL3Linear._prefill, linear.py:97-105).
+    Raises RuntimeError once an earlier launch on this device reported a timed-out wait."""
     M = xh.shape[0]
     _need_cuda(xh, trellis_u32, svh)
     if xh.dtype != torch.float16:
@@ -349,14 +371,23 @@ def gemm(xh: torch.Tensor, trellis_u32: torch.Tensor, k: int, n: int, K: int, cb
     if trellis_u32.numel() * trellis_u32.element_size() != k * n * K // 8:
         raise ValueError(f"trellis holds {trellis_u32.numel() * trellis_u32.element_size()} bytes, "
                          f"expected {k * n * K // 8} for {k}x{n} at {K} bpw")
+    st = _status(xh.device)
+    st.before_launch()
     xh = xh.contiguous()
     svh = svh.to(torch.float16).reshape(-1).contiguous()
     y = out if out is not None else torch.empty((M, n), dtype=out_dtype, device=xh.device)
     check(lib().exl3_gemm(xh.data_ptr(), M, k, n, trellis_u32.data_ptr(), K, cb, svh.data_ptr(), y.data_ptr(),
-                          dtype_code(y.dtype), _status(xh.device).data_ptr(), stream_ptr(xh.device)), "exl3_gemm")
+                          dtype_code(y.dtype), st.word.data_ptr(), stream_ptr(xh.device)), "exl3_gemm")
+    st.after_launch()
     return y
 
 
 def gemm_status(device: torch.device | None = None) -> int:
-    """The prefill kernel's error word on `device` (0 = no bounded wait ever gave up)."""
-    return int(_status(device or torch.device("cuda", torch.cuda.current_device()))[0].item())
+    """The prefill kernel's error word on `device` (0 = no bounded wait ever gave up); synchronises."""
+    return _status(device or torch.device("cuda", torch.cuda.current_device())).read()
+
+
+def check_gemm_status(device: torch.device | None = None) -> None:
+    """Raise RuntimeError if a prefill GEMM on `device` ever reported a timed-out wait (synchronises)."""
+    st = _status(device or torch.device("cuda", torch.cuda.current_device()))
+    st.raise_if_set(st.read())

@@ -1,21 +1,30 @@
-"""EXL3 linear layers for PyTorch on B200: the drop-in for the reference's linear.py.
+"""PyTorch modules for EXL3-quantised linears, backed by the sm_100a kernels of this package.
 
-Mirrors daig/omlx-exl3 src/omlx/exl3/linear.py. EXL3Linear holds exactly the checkpoint tensors of
-one ExLlamaV3 linear (trellis, suh/su, svh/sv, mul1/mcg marker, optional bias) as module buffers
-named after the checkpoint parts, so strict state-dict loading fills it like any layer. Forward
-computes  y = had128( had128(x * suh) @ W_inner ) * svh  (+ bias):
+An EXL3 checkpoint stores each quantised linear as a handful of tensors under one prefix: the
+trellis bitstream (int16, [k/16, n/16, 16*bits]), the input and output sign vectors (fp16 `suh` /
+`svh`, or the older bit-packed int16 `su` / `sv`), an optional codebook marker (`mul1` or `mcg`; its
+presence is what matters) and an optional bias. `EXL3Linear` registers exactly the tensors the
+checkpoint declares, under those names, so loading a state dict fills it without any renaming.
 
-  rows <= MAX_GEMV_ROWS (decode, speculative verify): the input rotation (one kernel, or none when
-      the producer primed it, see fusion.py), then one trellis GEMV kernel that also reduces, applies
-      the output rotation and svh, and writes the caller's dtype (kernels.TrellisGemvPlan)
-  more rows (prefill): input rotation, trellis decode, fp16 GEMM, output rotation and svh
-      (prefill.py)
+The product it computes, for an input x of any leading shape, is
 
-EXL3SiblingGroup runs same-input siblings (q/k/v, gate/up, in_proj_qkv/z) as one GEMV launch over
-their own trellis buffers when they share K and codebook; each member returns its slice, served from
-a single-slot cache keyed on the input tensor's identity.
+    y = H(H(x * suh) @ W) * svh  (+ bias)          H: 128-point Walsh-Hadamard blocks scaled by 1/sqrt(128)
+
+where W is the k x n matrix the trellis decodes to. Up to MAX_GEMV_ROWS rows (batch decode, speculative
+verify) the input rotation is one kernel (skipped when a fused producer has already written it, see
+`prime`) and the rest is one GEMV launch that decodes the trellis on the fly. Larger inputs take the
+prefill path (prefill.py).
+
+`EXL3SiblingGroup` ties 2-3 linears that read the same input (q/k/v, gate/up, in_proj_qkv/z) into a
+single GEMV launch over their separate trellis buffers.
+
+Reference: daig/omlx-exl3 src/omlx/exl3/linear.py (EXL3Linear :43-121, EXL3SiblingGroup :124-193);
+constructor, buffer names, forward signature and the fusion hooks (rot_suh, prime, gemv_rotated,
+fusable, gemv) are kept as there.
 """
 from __future__ import annotations
+
+from dataclasses import dataclass
 
 import torch
 from torch import nn
@@ -27,169 +36,202 @@ PREFILL_COL_CHUNK = 16384          # output columns decoded per chunk on the unf
 
 
 def unpack_signs(bits: torch.Tensor) -> torch.Tensor:
-    """Packed int16 sign bitfield (legacy su/sv) -> +-1 fp16 vector, bit i of word j = element 16j+i
-    (linear.py:36-40)."""
-    b = bits.reshape(-1).view(torch.int16).to(torch.int32) & 0xFFFF
-    expanded = (b[:, None] >> torch.arange(16, dtype=torch.int32, device=bits.device)) & 1
-    return (1.0 - 2.0 * expanded.reshape(-1).to(torch.float32)).to(torch.float16)
+    """Legacy packed sign vector -> +-1 fp16. Word j of the int16 bitfield carries elements 16j..16j+15,
+    least significant bit first; a set bit means -1 (reference linear.py:36-40)."""
+    words = bits.reshape(-1).view(torch.int16).to(torch.int32) & 0xFFFF
+    shifts = torch.arange(16, dtype=torch.int32, device=bits.device)
+    neg = ((words.unsqueeze(1) >> shifts) & 1).reshape(-1)
+    return torch.where(neg.bool(), -1.0, 1.0).to(torch.float16)
+
+
+def trellis_bitrate(trellis: torch.Tensor) -> int:
+    """Bits per weight of a trellis tensor: each 16x16 tile holds 256*K bits = 16*K int16 words."""
+    words = int(trellis.shape[-1])
+    if words % 16:
+        raise NotImplementedError(f"EXL3 tensor at {words / 16} bpw: half-integer bitrates are not supported")
+    return words // 16
+
+
+@dataclass
+class _Runtime:
+    """What the kernels need from a loaded EXL3Linear, derived once from its checkpoint tensors."""
+    bits: int
+    codebook: int                  # 0 = 3inst (no marker), 1 = mcg, 2 = mul1
+    suh: torch.Tensor              # (k,) fp16
+    svh: torch.Tensor              # (n,) fp16
+    words: torch.Tensor            # trellis as a flat int32 view (the kernels read uint32 words)
+    plans: dict
 
 
 class EXL3Linear(nn.Module):
     def __init__(self, in_features: int, out_features: int, tensors: dict[str, tuple[tuple[int, ...], torch.dtype]],
                  device: torch.device | str | None = None):
-        """tensors: checkpoint tensor name (trellis, suh, svh, su, sv, mul1, mcg, bias) -> (shape, dtype)."""
+        """tensors maps each checkpoint part present for this linear (trellis, suh / su, svh / sv, mul1 /
+        mcg, bias) to its (shape, dtype); a zero buffer of that shape is registered under the part's name."""
         super().__init__()
         self.in_features, self.out_features = in_features, out_features
-        for name, (shape, dtype) in tensors.items():
-            self.register_buffer(name, torch.zeros(shape, dtype=dtype, device=device))
-        self._group = None
-        self._idx = 0
-        self._ready = False
-        self._primed = None
+        for part, (shape, dtype) in tensors.items():
+            self.register_buffer(part, torch.zeros(shape, dtype=dtype, device=device))
+        self._rt: _Runtime | None = None
+        self._group = None           # EXL3SiblingGroup this linear belongs to, if any
+        self._idx = 0                # its position in that group
+        self._primed = None          # (input tensor, its rotation) handed over by a fused producer
 
-    def __contains__(self, name: str) -> bool:
-        """`"mul1" in linear`: whether the checkpoint declared that part (MLX module semantics)."""
-        return name in self._buffers and self._buffers[name] is not None
+    def __contains__(self, part: str) -> bool:
+        """Whether the checkpoint declared `part` for this linear (e.g. `"mul1" in lin`)."""
+        return self._buffers.get(part) is not None
 
-    # -- runtime state, derived once from the loaded tensors -------------------------------------
-    def _prepare(self):
-        if self._ready:
-            return
-        w16 = self.trellis.shape[-1]
-        if w16 % 16:
-            raise NotImplementedError(f"half-integer EXL3 bitrate ({w16 / 16} bpw) is not supported yet")
-        self._K = w16 // 16
-        self._cb = 2 if "mul1" in self else 1 if "mcg" in self else 0
-        suh = self.suh if "suh" in self else unpack_signs(self.su)
-        svh = self.svh if "svh" in self else unpack_signs(self.sv)
-        self._suh = suh.to(torch.float16).reshape(-1).contiguous()
-        self._svh = svh.to(torch.float16).reshape(-1).contiguous()
-        self._suh2d = self._suh.reshape(1, -1)
-        self._tr = self.trellis.contiguous().view(torch.int32).reshape(-1)
-        self._plans = {}
-        self._ready = True
+    # -- derived state ---------------------------------------------------------------------------
+    def runtime(self) -> _Runtime:
+        """Bitrate, codebook, fp16 sign vectors and the trellis word view, computed on first use."""
+        if self._rt is None:
+            marker = next((m for m in ("mul1", "mcg") if m in self), None)
+            signs_in = self.suh if "suh" in self else unpack_signs(self.su)
+            signs_out = self.svh if "svh" in self else unpack_signs(self.sv)
+            self._rt = _Runtime(bits=trellis_bitrate(self.trellis), codebook={"mul1": 2, "mcg": 1, None: 0}[marker],
+                                suh=signs_in.reshape(-1).to(torch.float16).contiguous(),
+                                svh=signs_out.reshape(-1).to(torch.float16).contiguous(),
+                                words=self.trellis.contiguous().view(torch.int32).reshape(-1), plans={})
+        return self._rt
 
     def reset_runtime(self):
-        """Drop derived state (after the buffers were replaced or moved)."""
-        self._ready = False
+        """Forget the derived state (call after the buffers were replaced, reloaded or moved)."""
+        self._rt = None
         self._primed = None
 
     @property
+    def bits(self) -> int:
+        return self.runtime().bits
+
+    @property
+    def codebook(self) -> int:
+        return self.runtime().codebook
+
+    @property
+    def trellis_words(self) -> torch.Tensor:
+        return self.runtime().words
+
+    @property
+    def output_signs(self) -> torch.Tensor:
+        return self.runtime().svh
+
+    # -- fusion hooks ----------------------------------------------------------------------------
+    @property
     def rot_suh(self) -> torch.Tensor:
-        """(1, in_features): this linear's input scales, as rotation kernels take them."""
-        self._prepare()
-        return self._suh2d
+        """Input sign vector shaped (1, in_features): the `suh` operand of the rotation kernels."""
+        return self.runtime().suh.view(1, -1)
 
     def prime(self, x: torch.Tensor, xh: torch.Tensor):
-        """The next call with exactly this tensor uses xh as its rotated input (fusion.py)."""
+        """Hand over xh = H(x * suh) computed by a fused producer; used only if the next forward gets
+        this very tensor object x."""
         self._primed = (x, xh)
 
+    def _take_primed(self, x: torch.Tensor) -> torch.Tensor | None:
+        handed, self._primed = self._primed, None
+        return handed[1] if handed is not None and handed[0] is x else None
+
     def plan(self, rows: int, out_dtype: torch.dtype) -> TrellisGemvPlan:
-        self._prepare()
-        plan = self._plans.get((rows, out_dtype))
-        if plan is None:
-            plan = self._plans[(rows, out_dtype)] = TrellisGemvPlan(
-                self.in_features, [self.out_features], self._K, self._cb, self._svh, rows, out_dtype)
-        return plan
+        rt = self.runtime()
+        key = (rows, out_dtype)
+        if key not in rt.plans:
+            rt.plans[key] = TrellisGemvPlan(self.in_features, [self.out_features], rt.bits, rt.codebook, rt.svh,
+                                            rows, out_dtype)
+        return rt.plans[key]
 
     def gemv_rotated(self, xh: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
-        """(rows, out_features) from an already rotated input xh, (1, rows, k) or (rows, k)."""
-        rows = xh.shape[-2]
-        return self.plan(rows, out_dtype)(xh, [self._tr])
+        """GEMV of an input already rotated by H(. * suh): xh (1, rows, k) or (rows, k) fp16 ->
+        (rows, out_features) in out_dtype."""
+        return self.plan(xh.shape[-2], out_dtype)(xh, [self.trellis_words])
 
-    def _bias(self, y):
-        return y + self.bias.to(y.dtype) if "bias" in self else y
-
-    def _prefill(self, x2: torch.Tensor) -> torch.Tensor:
-        return prefill.linear_prefill(x2, self._tr, self.in_features, self.out_features, self._K, self._cb,
-                                      self._suh, self._svh)
-
+    # -- forward ---------------------------------------------------------------------------------
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._group is not None:
             return self._group.member_output(x, self._idx)
-        self._prepare()
-        in_shape, dtype = x.shape, x.dtype
-        rows = x.numel() // self.in_features
-        if rows <= MAX_GEMV_ROWS:
-            primed, self._primed = self._primed, None
-            xh = primed[1] if primed is not None and primed[0] is x else \
-                rot(x.reshape(rows, self.in_features), self.rot_suh)
-            y = self.gemv_rotated(xh, dtype if dtype in (torch.float16, torch.bfloat16) else torch.float16)
-            y = y.to(dtype)
+        rt = self.runtime()
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.in_features)
+        if x2.shape[0] > MAX_GEMV_ROWS:
+            y = prefill.linear_prefill(x2, rt.words, self.in_features, self.out_features, rt.bits, rt.codebook,
+                                       rt.suh, rt.svh)
         else:
-            y = self._prefill(x.reshape(rows, self.in_features)).to(dtype)
-        return self._bias(y).reshape(in_shape[:-1] + (self.out_features,))
+            xh = self._take_primed(x)
+            if xh is None:
+                xh = rot(x2, self.rot_suh)
+            gemv_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
+            y = self.gemv_rotated(xh, gemv_dtype)
+        y = y.to(x.dtype)
+        if "bias" in self:
+            y = y + self.bias.to(y.dtype)
+        return y.reshape(*lead, self.out_features)
 
 
 class EXL3SiblingGroup:
-    """Same-input EXL3 siblings computed in one launch (rows <= MAX_GEMV_ROWS)."""
+    """2-3 EXL3 linears fed by one input, computed by one GEMV launch for rows <= MAX_GEMV_ROWS.
+
+    Eligible members share in_features, bitrate and codebook, have output widths that are multiples
+    of 128 and no bias (`fusable`). Joining a group redirects each member's forward here: the first
+    member called with an input runs the group's launch, and the other members take their column
+    slice of that result for the same input.
+    """
 
     def __init__(self, members: list[EXL3Linear]):
-        for m in members:
-            m._prepare()
-        first = members[0]
-        self.members = members
-        self.k = first.in_features
+        rts = [m.runtime() for m in members]
+        self.members = list(members)
+        self.k = members[0].in_features
         self.ns = [m.out_features for m in members]
-        self.K, self.cb = first._K, first._cb
-        self.suh = torch.stack([m._suh for m in members]).contiguous()          # (n_members, k)
-        self.svh = torch.cat([m._svh for m in members]).contiguous()
-        self.trs = [m._tr for m in members]
+        self.K, self.cb = rts[0].bits, rts[0].codebook
+        self.suh = torch.stack([rt.suh for rt in rts])               # (n_members, k): one rotation per member
+        self.svh = torch.cat([rt.svh for rt in rts])                 # output signs in member order
+        self.trs = [rt.words for rt in rts]
         self.plans: dict[tuple, TrellisGemvPlan] = {}
-        self._cache_x = None
-        self._cache_out = None
-        self._served: set[int] = set()
         self._primed = None
-        for i, m in enumerate(members):
-            m._group, m._idx = self, i
+        self._last: tuple | None = None        # (input, per-member outputs, members not yet served)
+        for idx, m in enumerate(members):
+            m._group, m._idx = self, idx
 
     @staticmethod
     def fusable(members: list[EXL3Linear]) -> bool:
-        for m in members:
-            m._prepare()
-        f = members[0]
-        return (2 <= len(members) <= 3
-                and all(m.in_features == f.in_features and m._K == f._K and m._cb == f._cb for m in members)
-                and all(m.out_features % 128 == 0 and "bias" not in m for m in members))
+        if not 2 <= len(members) <= 3:
+            return False
+        key = {(m.in_features, m.bits, m.codebook) for m in members}
+        return len(key) == 1 and not any(m.out_features % 128 or "bias" in m for m in members)
 
     @property
     def rot_suh(self) -> torch.Tensor:
         return self.suh
 
     def prime(self, x: torch.Tensor, xh: torch.Tensor):
-        """The next call with exactly this tensor uses xh (n_members, rows, k) as its rotated input."""
+        """Hand over the members' rotated inputs xh (n_members, rows, k) for the input tensor x."""
         self._primed = (x, xh)
 
     def plan(self, rows: int, out_dtype: torch.dtype) -> TrellisGemvPlan:
-        plan = self.plans.get((rows, out_dtype))
-        if plan is None:
-            plan = self.plans[(rows, out_dtype)] = TrellisGemvPlan(self.k, self.ns, self.K, self.cb, self.svh,
-                                                                   rows, out_dtype)
-        return plan
+        key = (rows, out_dtype)
+        if key not in self.plans:
+            self.plans[key] = TrellisGemvPlan(self.k, self.ns, self.K, self.cb, self.svh, rows, out_dtype)
+        return self.plans[key]
 
     def gemv(self, x: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
-        """All members' outputs, concatenated: (rows, sum(ns)) in out_dtype (rows <= MAX_GEMV_ROWS)."""
-        rows = x.numel() // self.k
-        primed, self._primed = self._primed, None
-        xh = primed[1] if primed is not None and primed[0] is x else rot(x.reshape(rows, self.k), self.suh)
-        return self.plan(rows, out_dtype)(xh, self.trs)
+        """One launch for all members: (rows, sum(ns)) in out_dtype, members side by side."""
+        handed, self._primed = self._primed, None
+        x2 = x.reshape(-1, self.k)
+        xh = handed[1] if handed is not None and handed[0] is x else rot(x2, self.suh)
+        return self.plan(x2.shape[0], out_dtype)(xh, self.trs)
 
     def member_output(self, x: torch.Tensor, idx: int) -> torch.Tensor:
-        """Member idx's output. The group computes once per input and serves each member once from
-        the cache (torch tensors are mutable, so a cached result is not reused for a later call)."""
-        if self._cache_x is x and idx not in self._served:
-            self._served.add(idx)
-            return self._cache_out[idx]
-        out = self(x)
-        self._served = {idx}
-        return out[idx]
+        """Output of member idx for input x. A group result is handed to each member once: tensors are
+        mutable, so the same object passed again later (a reused static buffer) is recomputed."""
+        if self._last is not None and self._last[0] is x and idx in self._last[2]:
+            self._last[2].discard(idx)
+            return self._last[1][idx]
+        outs = self(x)
+        self._last = (x, outs, set(range(len(self.members))) - {idx})
+        return outs[idx]
 
     def __call__(self, x: torch.Tensor) -> tuple[torch.Tensor, ...]:
-        if self._cache_x is x and not self._served:
-            return self._cache_out
-        in_shape, dtype = x.shape, x.dtype
+        lead = x.shape[:-1]
         rows = x.numel() // self.k
-        if rows > MAX_GEMV_ROWS:   # prefill: each member on its own path
+        if rows > MAX_GEMV_ROWS:
+            # prefill: every member on its own path (detached from the group for the call)
             outs = []
             for m in self.members:
                 m._group = None
@@ -197,11 +239,7 @@ class EXL3SiblingGroup:
                     outs.append(m(x))
                 finally:
                     m._group = self
-            out = tuple(outs)
-        else:
-            odt = dtype if dtype in (torch.float16, torch.bfloat16) else torch.float16
-            y = self.gemv(x, odt).to(dtype)
-            out = tuple(o.reshape(in_shape[:-1] + (n,)) for o, n in zip(torch.split(y, self.ns, dim=-1), self.ns))
-        self._cache_x, self._cache_out = x, out
-        self._served = set()
-        return out
+            return tuple(outs)
+        gemv_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
+        y = self.gemv(x, gemv_dtype).to(x.dtype)
+        return tuple(part.reshape(*lead, n) for part, n in zip(y.split(self.ns, dim=-1), self.ns))

@@ -1,12 +1,12 @@
 """Place EXL3 checkpoints (or seeded synthetic EXL3 tensors) in HBM, sharded across the GPUs of a box.
 
-Mirrors daig/omlx-exl3 src/omlx/exl3/loader.py where the behaviour carries over:
-  is_exl3_config      loader.py:45-47    quantization_config.quant_method == "exl3"
-  _read_header        loader.py:50-55    safetensors JSON header (8-byte little-endian length)
-  inventory           loader.py:58-72    EXL3 linear prefix -> {part: (shape, dtype)} from headers only
-  group_siblings      loader.py:137-156  q/k/v, gate/up, in_proj_qkv/z grouped by (K, codebook)
-  unify_float_dtypes  loader.py:159-180  non-EXL3 float params cast to the embedding dtype
-  load                loader.py:183-223  build model, swap EXL3 linears, strict load, group, fuse
+Functions with a counterpart in daig/omlx-exl3 src/omlx/exl3/loader.py (same names and results):
+  is_exl3_config      loader.py:45-47    does config.json declare EXL3 quantisation
+  _read_header        loader.py:50-55    tensor table of one safetensors shard
+  inventory           loader.py:58-72    EXL3 linear prefix -> {part: (shape, dtype)}, from headers only
+  group_siblings      loader.py:137-156  same-input linears tied into single-launch groups per rate
+  unify_float_dtypes  loader.py:159-180  non-EXL3 float parameters at the embedding dtype
+  load                loader.py:183-223  model with EXL3 linears from a checkpoint directory
 The model is this package's Qwen3-style decoder (model.py) instead of mlx-vlm's, and load() takes the
 tensor-parallel rank and size: column-parallel linears (q/k/v, gate/up, lm_head) get whole 128-column
 blocks of the trellis ([:, nt0:nt1, :]) and of svh; row-parallel ones (o_proj, down_proj) get whole
@@ -41,78 +41,78 @@ ROW_PARALLEL = ("o_proj", "down_proj")
 
 
 def is_exl3_config(config: dict[str, Any]) -> bool:
-    qc = config.get("quantization_config") or {}
-    return str(qc.get("quant_method", "")).lower() == "exl3"
+    """Whether a Hugging Face config.json declares EXL3 quantisation (quant_method "exl3", any case)."""
+    method = (config.get("quantization_config") or {}).get("quant_method")
+    return isinstance(method, str) and method.casefold() == "exl3"
 
 
 def _read_header(path: Path) -> dict[str, Any]:
+    """Tensor table of one safetensors file: a little-endian u64 byte count, then that many bytes of
+    JSON mapping each tensor name to its dtype, shape and offsets (the `__metadata__` entry dropped)."""
     with open(path, "rb") as fh:
-        n = struct.unpack("<Q", fh.read(8))[0]
-        header = json.loads(fh.read(n))
-    header.pop("__metadata__", None)
-    return header
+        (size,) = struct.unpack("<Q", fh.read(8))
+        table = json.loads(fh.read(size).decode("utf-8"))
+    return {name: entry for name, entry in table.items() if name != "__metadata__"}
 
 
 def _files(model_path: Path) -> list[str]:
+    """The checkpoint's safetensors shards: those the index names, else the single model.safetensors."""
     index = model_path / "model.safetensors.index.json"
-    return sorted(set(json.loads(index.read_text())["weight_map"].values())) if index.exists() \
-        else ["model.safetensors"]
+    if not index.exists():
+        return ["model.safetensors"]
+    return sorted(set(json.loads(index.read_text())["weight_map"].values()))
 
 
 def inventory(model_path: Path) -> dict[str, dict[str, tuple[tuple[int, ...], Any]]]:
-    """EXL3 linear prefix (checkpoint naming) -> {part: (shape, dtype)}."""
-    headers: dict[str, Any] = {}
+    """For every EXL3 linear of the checkpoint (a tensor name prefix with a `.trellis` part), the parts
+    present (`_EXL3_PARTS`) with their (shape, torch dtype), read from the shard headers only."""
+    parts_by_prefix: dict[str, dict[str, tuple[tuple[int, ...], Any]]] = {}
     for f in _files(model_path):
-        headers.update(_read_header(model_path / f))
-    inv: dict[str, dict[str, tuple[tuple[int, ...], Any]]] = {}
-    for key in headers:
-        if key.endswith(".trellis"):
-            prefix = key[: -len(".trellis")]
-            inv[prefix] = {part: (tuple(headers[f"{prefix}.{part}"]["shape"]), _DTYPES[headers[f"{prefix}.{part}"]["dtype"]])
-                           for part in _EXL3_PARTS if f"{prefix}.{part}" in headers}
-    return inv
+        for name, entry in _read_header(model_path / f).items():
+            prefix, _, part = name.rpartition(".")
+            if part in _EXL3_PARTS:
+                parts_by_prefix.setdefault(prefix, {})[part] = (tuple(entry["shape"]), _DTYPES[entry["dtype"]])
+    return {prefix: parts for prefix, parts in parts_by_prefix.items() if "trellis" in parts}
+
+
+def _sibling_sets(model: torch.nn.Module):
+    """Every complete set of same-input EXL3 linears (one of _SIBLINGS found under one module)."""
+    for _, owner in model.named_modules():
+        for names in _SIBLINGS:
+            found = [getattr(owner, nm, None) for nm in names]
+            if all(isinstance(lin, EXL3Linear) for lin in found):
+                yield found
 
 
 def group_siblings(model: torch.nn.Module) -> int:
-    """Group same-input EXL3 siblings (q/k/v, gate/up, in_proj_qkv/z) into single-launch groups. One
-    launch needs one bitrate, so siblings are partitioned by (bitrate, codebook)."""
-    groups = 0
-    for _, module in model.named_modules():
-        for names in _SIBLINGS:
-            members = [getattr(module, n, None) for n in names]
-            if not all(isinstance(m, EXL3Linear) for m in members):
-                continue
-            for m in members:
-                m._prepare()
-            by_rate: dict = {}
-            for m in members:
-                by_rate.setdefault((m._K, m._cb), []).append(m)
-            for subset in by_rate.values():
-                if EXL3SiblingGroup.fusable(subset):
-                    EXL3SiblingGroup(subset)
-                    groups += 1
-    return groups
+    """Tie same-input EXL3 linears into EXL3SiblingGroups (one GEMV launch each). A group launch runs
+    one bitrate and codebook, so a set is first split by (bits, codebook): a checkpoint that gives q
+    its own rate still gets k and v as a pair. Returns the number of groups made."""
+    made = 0
+    for found in _sibling_sets(model):
+        rates = sorted({(lin.bits, lin.codebook) for lin in found})
+        for rate in rates:
+            subset = [lin for lin in found if (lin.bits, lin.codebook) == rate]
+            if EXL3SiblingGroup.fusable(subset):
+                EXL3SiblingGroup(subset)
+                made += 1
+    return made
 
 
 def unify_float_dtypes(model: torch.nn.Module) -> int:
-    """Cast non-EXL3 floating parameters/buffers to the embedding dtype (EXL3Linear computes in fp16
-    internally and returns the caller's dtype, so it is left alone)."""
-    target = None
-    for name, m in model.named_modules():
-        if name.endswith("embed_tokens") and hasattr(m, "weight"):
-            target = m.weight.dtype
-            break
-    if target is None:
+    """Bring every floating-point parameter outside the EXL3 linears to the token embedding's dtype, so
+    no elementwise op mixes fp16 and bf16 operands (which would promote to fp32). EXL3Linear keeps its
+    checkpoint dtypes: it computes in fp16 internally and returns its caller's dtype. Returns the
+    number of parameters cast."""
+    embed = next((m for name, m in model.named_modules() if name.endswith("embed_tokens")), None)
+    if embed is None or getattr(embed, "weight", None) is None:
         return 0
-    n = 0
-    for name, m in model.named_modules():
-        if isinstance(m, EXL3Linear):
-            continue
-        for pname, p in list(m.named_parameters(recurse=False)):
-            if p.dtype.is_floating_point and p.dtype != target:
-                p.data = p.data.to(target)
-                n += 1
-    return n
+    want = embed.weight.dtype
+    casts = [p for m in model.modules() if not isinstance(m, EXL3Linear)
+             for p in m.parameters(recurse=False) if p.dtype.is_floating_point and p.dtype != want]
+    for p in casts:
+        p.data = p.data.to(want)
+    return len(casts)
 
 
 # ------------------------------------------------------------------------------ shard helpers

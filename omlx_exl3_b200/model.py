@@ -254,24 +254,20 @@ class _MixedGroup:
     list of K); for q/k/v the decode step still finishes with qkv_post's math in that launch."""
 
     def __init__(self, members: list[EXL3Linear]):
-        for m in members:
-            m._prepare()
         self.members = members
         self.k = members[0].in_features
         self.ns = [m.out_features for m in members]
-        self.Ks = [m._K for m in members]
-        self.cb = members[0]._cb
+        self.Ks = [m.bits for m in members]
+        self.cb = members[0].codebook
         self.rot_suh = torch.cat([m.rot_suh for m in members]).contiguous()     # (3, k)
-        self.svh = torch.cat([m._svh for m in members]).contiguous()
-        self.trs = [m._tr for m in members]
+        self.svh = torch.cat([m.output_signs for m in members]).contiguous()
+        self.trs = [m.trellis_words for m in members]
         self.plans: dict[tuple, TrellisGemvPlan] = {}
 
     @staticmethod
     def fits(members: list[EXL3Linear]) -> bool:
-        for m in members:
-            m._prepare()
         f = members[0]
-        return all(m.in_features == f.in_features and m._cb == f._cb and "bias" not in m and
+        return all(m.in_features == f.in_features and m.codebook == f.codebook and "bias" not in m and
                    m.out_features % 128 == 0 for m in members)
 
     def plan(self, rows: int, out_dtype: torch.dtype) -> TrellisGemvPlan:
@@ -416,7 +412,7 @@ class Qwen3EXL3(nn.Module):
             nonlocal slot
             if peers is None:
                 return self.tp.all_reduce(lin.gemv_rotated(xh_in, dt))
-            lin.plan(rows, dt).peer(xh_in, [lin._tr], peers, slot)   # pushed into every rank's inbox
+            lin.plan(rows, dt).peer(xh_in, [lin.trellis_words], peers, slot)   # pushed into every rank's inbox
             slot ^= 1
             return slot ^ 1
 
@@ -504,9 +500,13 @@ class Qwen3EXL3(nn.Module):
         return out[:, : self.cfg.vocab_size]
 
     def greedy(self, local: torch.Tensor) -> torch.Tensor:
-        """Global argmax token per row from the local logit shard (one small all-gather)."""
-        v0 = self.vocab_range[0]
-        n_valid = self.vocab_range[1] - v0
+        """Global argmax token per row from the local logit shard (one small all-gather). Without an
+        output head the argmax is over the (replicated) final hidden state."""
+        if self.lm_head is None:
+            v0, n_valid = 0, local.shape[1]
+        else:
+            v0 = self.vocab_range[0]
+            n_valid = self.vocab_range[1] - v0
         val, idx = argmax(local, n_valid, v0)                           # one pass over the fp16/bf16 logits
         if self.tp.size == 1:
             return idx

@@ -9,9 +9,10 @@ CPU, used to pin oracle/exl3_oracle.c and to generate the golden fixtures in tes
 holds the timed CPU baseline of bench.py (`--impl reference`): the reference decode, then an fp32
 GEMV and the 128-point output rotation.
 
-Generated sources and the library go to oracle/_ref/ only (git-ignored). Needs the reference checkout
-(EXL3_REFERENCE_ROOT, default: the reference checkout's path in the build container); the GPU box
-uses the prebuilt library.
+Generated sources and the library go to oracle/_ref/ only (git-ignored). Needs a read-only checkout of
+the reference: the directory named by EXL3_REFERENCE_ROOT, else a `reference` directory beside this
+repository's root. Without one, build() keeps an existing library and otherwise builds nothing; the
+GPU box uses the prebuilt library.
 """
 from __future__ import annotations
 
@@ -25,7 +26,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 LIB = OUT / "libexl3_ref.so"
-REF_ROOT = Path(os.environ.get("EXL3_REFERENCE_ROOT", "/" + "root/reference"))
+REF_ROOT = Path(os.environ["EXL3_REFERENCE_ROOT"]) if os.environ.get("EXL3_REFERENCE_ROOT") \
+    else HERE.parent.parent / "reference"
 KERNELS_PY = REF_ROOT / "src" / "omlx" / "exl3" / "kernels.py"
 
 

@@ -101,7 +101,7 @@ def test_gemv_peer_feeds_ar(cuda, dtype, rows):
             torch.cuda.synchronize()
             _check(h, xn, xh, eh, exn, suh)
             assert torch.equal(h1, h)
-        assert A.status() == 0 and plan.workspace_status() == 0
+        assert A.status() == 0 and int(plan.counters.abs().sum().item()) == 0
     finally:
         A.close()
         B.close()

@@ -19,13 +19,13 @@ def _t(t: np.ndarray, dev):
     return torch.from_numpy(O.trellis_u32(t).view(np.int32).copy()).to(dev)
 
 
-def _run(dev, k, ns, K, cb, rows, out_dtype, seed=0, bit31=False, svh_scale=0.01, row_exact=None):
+def _run(dev, k, ns, K, cb, rows, out_dtype, seed=0, bit31=False, svh_scale=0.01):
     from omlx_exl3_b200.kernels import TrellisGemvPlan
     rng = np.random.default_rng(seed)
     trs = [O.random_trellis(k, n, K, seed * 10 + i, bit31=bit31) for i, n in enumerate(ns)]
     svh = (rng.standard_normal(sum(ns)) * svh_scale).astype(np.float16)
     xh = rng.standard_normal((len(ns), rows, k)).astype(np.float16)
-    plan = TrellisGemvPlan(k, ns, K, cb, torch.from_numpy(svh).to(dev), rows, out_dtype, row_exact=row_exact)
+    plan = TrellisGemvPlan(k, ns, K, cb, torch.from_numpy(svh).to(dev), rows, out_dtype)
     y = plan(torch.from_numpy(xh).to(dev), [_t(t, dev) for t in trs])
     torch.cuda.synchronize()
     ref = O.gemv(trs, k, ns, K, cb, xh, svh)
@@ -42,13 +42,10 @@ def test_gemv_reference_cases(cuda, bits, ns):
     for rows in (1, 3, 8):
         for dt in (torch.float16, torch.bfloat16):
             y, ref, plan = _run(cuda, 1024, ns, bits, 2, rows, dt, seed=bits + rows, bit31=False)
-            if rows == 1:
-                yx, _, _ = _run(cuda, 1024, ns, bits, 2, rows, dt, seed=bits + rows, bit31=False, row_exact=True)
-                assert O.max_rel(yx.float().cpu().numpy(), ref) < TOL[dt]
             assert y.dtype == dt and tuple(y.shape) == (rows, sum(ns))
             e = O.max_rel(y.float().cpu().numpy(), ref)
             assert e < TOL[dt], (bits, ns, rows, dt, e)
-            assert plan.workspace_status() == 0
+            assert int(plan.counters.abs().sum().item()) == 0
 
 
 @pytest.mark.parametrize("cb", [0, 1, 2])
@@ -89,8 +86,7 @@ def test_gemv_bench_shapes(cuda, k, n):
         tsub = t[:, : nc // 16, :].copy()
         ref = O.gemv_c(tsub, k, nc, K, 0, xh[0], svh[:nc])
         assert O.max_rel(y[:, :nc], ref) < TOL[torch.float16], (k, n, rows)
-        assert plan.workspace_status() == 0
-        assert int(plan.counters[:plan.blocks].abs().sum().item()) == 0
+        assert int(plan.counters.abs().sum().item()) == 0
 
 
 def test_gemv_deterministic_and_row_exact(cuda):
@@ -108,13 +104,32 @@ def test_gemv_deterministic_and_row_exact(cuda):
         pr = TrellisGemvPlan(k, [n], K, 0, svh, r, torch.float16)
         yr = pr(xh8[:, :r].contiguous(), [t])
         assert torch.equal(yr, a[:r]), r
-    # one row: row-exact on request, else the CUDA-core path (deterministic, within tolerance)
-    p1x = TrellisGemvPlan(k, [n], K, 0, svh, 1, torch.float16, row_exact=True)
-    assert torch.equal(p1x(xh8[:, :1].contiguous(), [t]), a[:1])
-    p1 = TrellisGemvPlan(k, [n], K, 0, svh, 1, torch.float16, row_exact=False)
-    y1 = p1(xh8[:, :1].contiguous(), [t])
-    assert torch.equal(y1, p1(xh8[:, :1].contiguous(), [t]))
-    assert O.max_rel(y1.float().cpu().numpy(), a[:1].float().cpu().numpy()) < 2e-3
+    # one row takes the same fp32-accumulating path: bitwise row 0 of the 8-row call
+    p1 = TrellisGemvPlan(k, [n], K, 0, svh, 1, torch.float16)
+    assert torch.equal(p1(xh8[:, :1].contiguous(), [t]), a[:1])
+
+
+# Worst case for the accumulation: the longest reduction of the 27B-class shapes (down_proj, k = 17408)
+# at batch 1, every bitrate of the sweep. The reference multiplies each fp16 weight by x with fp32 FMAs
+# into fp32 accumulators (src/omlx/exl3/kernels.py:215-218); here each product is exact and summed in
+# fp32 on the tensor cores, so the error against the fp32 oracle stays at the fp16 output rounding.
+WORST_TOL = 2e-3
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 5, 6, 8])
+def test_gemv_worst_case_accumulation(cuda, bits):
+    from omlx_exl3_b200.kernels import TrellisGemvPlan
+    rng = np.random.default_rng(900 + bits)
+    k, n, nc = 17408, 5120, 512
+    t = O.random_trellis(k, n, bits, 40 + bits)
+    svh = np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float16)
+    xh = rng.standard_normal((1, 1, k)).astype(np.float16)
+    plan = TrellisGemvPlan(k, [n], bits, 0, torch.from_numpy(svh).to(cuda), 1, torch.float16)
+    y = plan(torch.from_numpy(xh).to(cuda), [_t(t, cuda)]).float().cpu().numpy()
+    ref = O.gemv_c(t[:, : nc // 16, :].copy(), k, nc, bits, 0, xh[0], svh[:nc])
+    e = O.max_rel(y[:, :nc], ref)
+    print(f"k=17408 n=5120 K={bits} rows=1 max-rel {e:.3e}")
+    assert e < WORST_TOL, (bits, e)
 
 
 def test_gemv_small_grids_and_many_segments(cuda):

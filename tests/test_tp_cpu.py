@@ -123,9 +123,8 @@ def test_linear_prepare_on_cpu_tensors():
     from omlx_exl3_b200 import EXL3Linear
     lin = EXL3Linear(256, 128, {"trellis": ((16, 8, 64), torch.int16), "suh": ((256,), torch.float16),
                                 "svh": ((128,), torch.float16), "mul1": ((1,), torch.int32)})
-    lin._prepare()
-    assert lin._K == 4 and lin._cb == 2 and lin._suh.shape == (256,)
+    assert lin.bits == 4 and lin.codebook == 2 and lin.rot_suh.shape == (1, 256)
     half = EXL3Linear(256, 128, {"trellis": ((16, 8, 40), torch.int16), "suh": ((256,), torch.float16),
                                  "svh": ((128,), torch.float16)})
     with pytest.raises(NotImplementedError):
-        half._prepare()
+        half.runtime()
