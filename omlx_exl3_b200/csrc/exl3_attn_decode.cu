@@ -42,7 +42,8 @@ constexpr int kKStride = 320;             // bytes per K row in shared memory (2
 constexpr int kVStride = 272;             // bytes per V row (256 + 16)
 constexpr int kRowBytes = kKStride + kVStride;
 constexpr int kAttPart = 132;             // floats per (kv head, split, q vector): max, sum, 2 pad, O[128]
-constexpr int kAttMaxQ = 16;              // q vectors per kv head (two n8 tiles)
+constexpr int kAttMaxQ = 16;              // q vectors per CTA (two n8 tiles)
+constexpr int kAttMaxQGroups = 4;         // q groups of kAttMaxQ per kv head: rows x grp <= 64
 constexpr int kAttMaxSplits = 512;
 constexpr int kAttMaxCta = 384;           // positions per CTA (shared memory: 384 x 592 bytes)
 constexpr int kCombThreads = 256;
@@ -100,6 +101,8 @@ __global__ void __launch_bounds__(32 * kAttMaxWarps, 1) attn_split_kernel(const 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int g = lane >> 2, c = lane & 3;
     const int h = blockIdx.y, s = blockIdx.x;
+    // q vectors [qg0, qg0 + nql) of this kv head's group (q vector j = new row j / grp, head j % grp)
+    const int qg0 = kAttMaxQ * blockIdx.z, nql = min(kAttMaxQ, p.nq - qg0);
     const int ppw = p.ppw;
     uint8_t* kbuf = att_sm + (size_t)warp * ppw * kRowBytes;
     uint8_t* vbuf = kbuf + (size_t)ppw * kKStride;
@@ -140,24 +143,24 @@ __global__ void __launch_bounds__(32 * kAttMaxWarps, 1) attn_split_kernel(const 
     }
     cp_async_commit();
 
-    // Q^T as the B operand; q column j = 8 qt + g of n-tile qt
+    // Q^T as the B operand; q column jl = 8 qt + g of n-tile qt is q vector qg0 + jl
     uint32_t qb[NQT][8][2];
     int lim[NQT][2];                                         // last visible position of column 8 qt + 2c + e
 #pragma unroll
     for (int qt = 0; qt < NQT; ++qt) {
-        const int j = 8 * qt + g;
+        const int jl = 8 * qt + g, j = qg0 + jl;
         const __half* qv = p.q + ((size_t)(j / p.grp) * p.hq + (size_t)h * p.grp + j % p.grp) * 128;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             const int d0 = 8 * c + 32 * (ks >> 1) + 4 * (ks & 1);
-            const uint2 v = j < p.nq ? *reinterpret_cast<const uint2*>(qv + d0) : make_uint2(0, 0);
+            const uint2 v = jl < nql ? *reinterpret_cast<const uint2*>(qv + d0) : make_uint2(0, 0);
             qb[qt][ks][0] = v.x;
             qb[qt][ks][1] = v.y;
         }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             const int jj = 8 * qt + 2 * c + e;
-            lim[qt][e] = jj < p.nq ? p.T - p.rows + jj / p.grp : -1;
+            lim[qt][e] = jj < nql ? p.T - p.rows + (qg0 + jj) / p.grp : -1;
         }
     }
 
@@ -267,8 +270,8 @@ __global__ void __launch_bounds__(32 * kAttMaxWarps, 1) attn_split_kernel(const 
     for (int qt = 0; qt < NQT; ++qt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const int q = 8 * qt + 2 * c + e;
-            if (q >= p.nq) continue;
+            const int q = 8 * qt + 2 * c + e;                // local to this CTA's q group
+            if (q >= nql) continue;
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) {
                 ob[q * 128 + 8 * g + mt] = oacc[mt][qt][e];
@@ -281,7 +284,7 @@ __global__ void __launch_bounds__(32 * kAttMaxWarps, 1) attn_split_kernel(const 
         }
     __syncthreads();
     // per q vector: the CTA max, the warps' weights and the CTA sum (one thread each), then O per (q, d)
-    if (threadIdx.x < p.nq) {
+    if (threadIdx.x < nql) {
         const int q = threadIdx.x;
         float M = -INFINITY;
 #pragma unroll
@@ -296,18 +299,18 @@ __global__ void __launch_bounds__(32 * kAttMaxWarps, 1) attn_split_kernel(const 
                 wm[w][q] = f;                                // now the warp's weight
                 L += f * wl[w][q];
             }
-        float* dst = p.part + (((size_t)h * p.splits + s) * p.nq + q) * kAttPart;
+        float* dst = p.part + (((size_t)h * p.splits + s) * p.nq + qg0 + q) * kAttPart;
         dst[0] = M;
         dst[1] = L;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < p.nq * 128; i += blockDim.x) {
+    for (int i = threadIdx.x; i < nql * 128; i += blockDim.x) {
         const int q = i >> 7, d = i & 127;
         float O = 0.f;
 #pragma unroll
         for (int w = 0; w < kAttMaxWarps; ++w)
             if (w < nw) O += wm[w][q] * reinterpret_cast<const float*>(att_sm + (size_t)w * ppw * kRowBytes)[i];
-        p.part[(((size_t)h * p.splits + s) * p.nq + q) * kAttPart + 4 + d] = O;
+        p.part[(((size_t)h * p.splits + s) * p.nq + qg0 + q) * kAttPart + 4 + d] = O;
     }
 
 }
@@ -459,7 +462,7 @@ __global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const float*
 static int attn_check(int rows, int hq, int hkv, int max_len, int T)
 {
     if (rows < 1 || hq < 1 || hkv < 1 || hq % hkv || max_len < 1 || T < rows || T > max_len) return EXL3_E_SHAPE;
-    if (rows * (hq / hkv) > kAttMaxQ) return EXL3_E_SHAPE;
+    if (rows * (hq / hkv) > kAttMaxQ * kAttMaxQGroups) return EXL3_E_SHAPE;
     return EXL3_OK;
 }
 
@@ -523,8 +526,9 @@ extern "C" int exl3_attn_decode_rot(const void* q, const void* k_cache, const vo
     prm.ppw = ppw;
     prm.splits = splits;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (int e = nq <= 8 ? launch_pdl(attn_split_kernel<1>, dim3(splits, hkv), dim3(32 * nw), smem, s, prm)
-                        : launch_pdl(attn_split_kernel<2>, dim3(splits, hkv), dim3(32 * nw), smem, s, prm))
+    const dim3 grid(splits, hkv, (nq + kAttMaxQ - 1) / kAttMaxQ);
+    if (int e = nq <= 8 ? launch_pdl(attn_split_kernel<1>, grid, dim3(32 * nw), smem, s, prm)
+                        : launch_pdl(attn_split_kernel<2>, grid, dim3(32 * nw), smem, s, prm))
         return e;
     if (int e = launch_pdl(attn_combine_kernel, dim3(nq, hkv), dim3(kCombThreads), 0, s, static_cast<const float*>(prm.part),
                            splits, nq, grp, hq, static_cast<const __half*>(suh), static_cast<__half*>(xh)))

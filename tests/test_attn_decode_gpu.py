@@ -40,6 +40,10 @@ def _reference(q, kc, vc, T, suh):
     (3, 40, 8, 257, 300),        # three new rows (15 q vectors per kv head), causal among them
     (2, 16, 2, 50, 64),          # exactly one 16-row tile of q vectors
     (1, 8, 8, 33, 40),           # no grouping
+    (4, 40, 8, 4100, 4200),      # 4-token MTP verify at the 27B-class layer: 20 q vectors, two q groups
+    (8, 40, 8, 300, 320),        # 8-token verify: 40 q vectors, three q groups (the last one partial)
+    (4, 5, 1, 4100, 4200),       # 4-token verify at tensor-parallel 8
+    (6, 40, 8, 70, 80),          # 6 rows, 30 q vectors, positions end inside a step
 ])
 def test_attn_decode_rot_matches_fp32(cuda, rows, hq, hkv, T, max_len):
     from omlx_exl3_b200 import kernels
@@ -83,9 +87,30 @@ def test_attn_decode_rot_matches_sdpa_and_is_deterministic(cuda):
 
 
 def test_attn_rejects_wide_groups(cuda):
+    """Up to 64 q vectors per kv head (4 groups of 16): every MTP-verify width at GQA 5 fits; wider
+    groups are rejected with an error, not computed wrongly."""
     from omlx_exl3_b200 import kernels
-    assert kernels.attn_fits(1, 40, 8) and kernels.attn_fits(3, 40, 8) and not kernels.attn_fits(4, 40, 8)
-    q = torch.zeros((4, 40, 128), device=cuda).half()
+    assert kernels.attn_fits(8, 40, 8) and kernels.attn_fits(4, 40, 8) and not kernels.attn_fits(8, 72, 8)
+    q = torch.zeros((8, 72, 128), device=cuda).half()
     kc = torch.zeros((8, 64, 128), device=cuda).half()
     with pytest.raises(Exception):
-        kernels.attn_rot(q, kc, kc.clone(), 32, torch.ones(40 * 128, device=cuda).half())
+        kernels.attn_rot(q, kc, kc.clone(), 32, torch.ones(72 * 128, device=cuda).half())
+
+
+def test_attn_verify_rows_are_row_exact(cuda):
+    """Row r of a multi-row (verify) call equals a single-row call at the same position over the same
+    cache, bit for bit: every q vector is reduced over the same positions in the same order whatever
+    the number of rows, so MTP verification reproduces plain decoding."""
+    from omlx_exl3_b200 import kernels
+    g = torch.Generator(device=cuda)
+    g.manual_seed(21)
+    rows, hq, hkv, T, max_len = 4, 40, 8, 4100, 4200
+    q = torch.randn((rows, hq, 128), device=cuda, generator=g).half()
+    kc = torch.randn((hkv, max_len, 128), device=cuda, generator=g).half()
+    vc = torch.randn((hkv, max_len, 128), device=cuda, generator=g).half()
+    suh = (torch.randint(0, 2, (hq * 128,), device=cuda, generator=g) * 2 - 1).half()
+    multi = kernels.attn_rot(q, kc, vc, T, suh)
+    for r in range(rows):
+        one = kernels.attn_rot(q[r:r + 1].contiguous(), kc, vc, T - rows + 1 + r, suh)
+        torch.cuda.synchronize()
+        assert torch.equal(one[0, 0], multi[0, r]), r
