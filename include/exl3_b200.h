@@ -115,6 +115,30 @@ EXL3_API int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_
               void* y, float* partials, uint32_t* counters, void* stream);
 
 /*
+ * exl3_gemv whose rotated input is computed inside the same launch: each CTA rotates the 128-column
+ * k blocks its units read (the arithmetic of exl3_rot / exl3_swiglu_rot, bit-identical results) into
+ * its own region of the scratch `xs`, then runs the GEMV on them. Same scratch rules as exl3_gemv, plus
+ * xs of exl3_gemv_prologue_workspace bytes (16-byte aligned, no initial contents needed). k % 128 == 0;
+ * members of one bitrate (no member_bits).
+ *   exl3_gemv_rot:          xh[m] = rot(x, suh[m]) for x (rows, k) of x_dtype (EXL3_F16 / BF16 / F32)
+ *                           and suh fp16 (n_members, k). Replaces: kernels.rot + TrellisGemvPlan.__call__,
+ *                           the two launches of EXL3Linear's decode forward (src/omlx/exl3/linear.py:
+ *                           111-117, kernels.py:451-458) and EXL3SiblingGroup.gemv (linear.py:163-172).
+ *   exl3_gemv_swiglu:       xh = swiglu_rot(gu, suh) for gu = [gate | up] (rows, 2k) of gu_dtype, suh
+ *                           fp16 (k); one member. Replaces: kernels.swiglu_rot + down_proj's
+ *                           gemv_rotated in the fused MLP (src/omlx/exl3/fusion.py:288-295).
+ *   exl3_gemv_swiglu_peer:  the same with the output rows pushed into the peers' inboxes as
+ *                           exl3_gemv_peer does (the row-parallel down_proj of a tensor-parallel step).
+ */
+EXL3_API int exl3_gemv_prologue_workspace(const exl3_gemv_desc* desc, size_t* xs_bytes);
+EXL3_API int exl3_gemv_rot(const exl3_gemv_desc* desc, const void* x, int x_dtype, const void* suh,
+                           const uint32_t* const* trellis, const void* svh, void* y, float* partials,
+                           uint32_t* counters, void* xs, size_t xs_bytes, void* stream);
+EXL3_API int exl3_gemv_swiglu(const exl3_gemv_desc* desc, const void* gu, int gu_dtype, const void* suh,
+                              const uint32_t* const* trellis, const void* svh, void* y, float* partials,
+                              uint32_t* counters, void* xs, size_t xs_bytes, void* stream);
+
+/*
  * Input rotation for 1..3 members: xh[m, r, :] = fp16( had128(x[r, :] * suh[m, :]) / sqrt(128) ).
  * Replaces: kernels.rot (src/omlx/exl3/kernels.py:451-458). x: (rows, k) of x_dtype; suh: fp16
  * (n_members, k); xh: fp16 (n_members, rows, k); k % 128 == 0.
@@ -279,6 +303,12 @@ EXL3_API int exl3_peer_put(const exl3_peer_group* g, int slot, const void* src, 
 EXL3_API int exl3_gemv_peer(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
                             const void* svh, float* partials, uint32_t* counters, const exl3_peer_group* g, int slot,
                             void* stream);
+
+/* exl3_gemv_swiglu with exl3_gemv_peer's output (see exl3_gemv_swiglu above). */
+EXL3_API int exl3_gemv_swiglu_peer(const exl3_gemv_desc* desc, const void* gu, int gu_dtype, const void* suh,
+                                   const uint32_t* const* trellis, const void* svh, float* partials,
+                                   uint32_t* counters, void* xs, size_t xs_bytes, const exl3_peer_group* g,
+                                   int slot, void* stream);
 
 /*
  * All-reduce of the row-parallel partials fused with residual add + RMSNorm + input rotation:

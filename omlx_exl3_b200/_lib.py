@@ -89,6 +89,11 @@ SIGNATURES = {
     "exl3_peer_put": (_I, [ctypes.POINTER(PeerGroupDesc), _I, _P, _I, _I, _P]),
     "exl3_argmax": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "exl3_gemv_peer": (_I, [ctypes.POINTER(GemvDesc), _P, _P, _P, _P, _P, ctypes.POINTER(PeerGroupDesc), _I, _P]),
+    "exl3_gemv_prologue_workspace": (_I, [ctypes.POINTER(GemvDesc), ctypes.POINTER(_SZ)]),
+    "exl3_gemv_rot": (_I, [ctypes.POINTER(GemvDesc), _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "exl3_gemv_swiglu": (_I, [ctypes.POINTER(GemvDesc), _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "exl3_gemv_swiglu_peer": (_I, [ctypes.POINTER(GemvDesc), _P, _I, _P, _P, _P, _P, _P, _P, _SZ,
+                                   ctypes.POINTER(PeerGroupDesc), _I, _P]),
 }
 
 

@@ -160,19 +160,43 @@ extern "C" int exl3_gemv_reset(uint32_t* counters, size_t counter_bytes, void* s
                : EXL3_E_CUDA;
 }
 
+// Input computed inside the GEMV instead of a given xh (exl3_gemv_rot / exl3_gemv_swiglu*).
+struct GemvPrologue {
+    int kind;                // exl3::kProRot or exl3::kProSwiglu
+    const void* src;
+    int src_dtype;
+    const void* suh;
+    void* xs;
+    size_t xs_bytes;
+};
+
+static size_t prologue_bytes(const exl3_gemv_desc* d, const exl3::GemvLaunch& L)
+{
+    return (size_t)L.grid * d->n_members * d->rows * d->k * sizeof(__half);
+}
+
 static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
                        void* y, float* partials, uint32_t* counters, const exl3_qkv_post_args* post,
-                       const exl3_peer_group* peer, int slot, void* stream)
+                       const exl3_peer_group* peer, int slot, const GemvPrologue* pro, void* stream)
 {
     using namespace exl3;
     GemvLaunch L;
     if (int e = plan_gemv(desc, &L)) return e;
-    if (!xh || !trellis || !svh || (!y && !post && !peer) || !partials || !counters) return EXL3_E_NULL;
+    if ((!xh && !pro) || !trellis || !svh || (!y && !post && !peer) || !partials || !counters) return EXL3_E_NULL;
+    if (pro) {
+        if (!pro->src || !pro->suh || !pro->xs) return EXL3_E_NULL;
+        if (desc->k % 128 || L.mixed || post) return EXL3_E_SHAPE;
+        if (pro->src_dtype != EXL3_F16 && pro->src_dtype != EXL3_BF16 && pro->src_dtype != EXL3_F32)
+            return EXL3_E_DTYPE;
+        if (!aligned(pro->xs, 16) || !aligned(pro->suh, 2) || !aligned(pro->src, pro->src_dtype == EXL3_F32 ? 4 : 2))
+            return EXL3_E_ALIGN;
+        if (pro->xs_bytes < prologue_bytes(desc, L)) return EXL3_E_WORKSPACE;
+    }
     for (int m = 0; m < desc->n_members; ++m) {
         if (!trellis[m]) return EXL3_E_NULL;
         if (!aligned(trellis[m], 16)) return EXL3_E_ALIGN;
     }
-    if (!aligned(xh, 4) || !aligned(svh, 2) || !aligned(y, 2) || !aligned(partials, 16) || !aligned(counters, 4))
+    if ((!pro && !aligned(xh, 4)) || !aligned(svh, 2) || !aligned(y, 2) || !aligned(partials, 16) || !aligned(counters, 4))
         return EXL3_E_ALIGN;
     if (int e = check_device()) return e;
 
@@ -220,9 +244,57 @@ static int gemv_common(const exl3_gemv_desc* desc, const void* xh, const uint32_
         return post ? launch_gemv_seg<1>(desc->codebook, prm, L.grid, L.smem, s)
                     : launch_gemv_seg<0>(desc->codebook, prm, L.grid, L.smem, s);
     }
+    if (pro) {
+        prm.src = pro->src;
+        prm.src_dtype = pro->src_dtype;
+        prm.suh = static_cast<const __half*>(pro->suh);
+        prm.xs = static_cast<__half*>(pro->xs);
+        prm.xs_stride = (long long)desc->n_members * desc->rows * desc->k;
+        if (pro->kind == kProRot)
+            return peer ? EXL3_E_SHAPE : launch_gemv_epi<0, kProRot>(desc->bits, desc->codebook, prm, L.grid, s);
+        return peer ? launch_gemv_epi<2, kProSwiglu>(desc->bits, desc->codebook, prm, L.grid, s)
+                    : launch_gemv_epi<0, kProSwiglu>(desc->bits, desc->codebook, prm, L.grid, s);
+    }
     if (post) return launch_gemv_epi<1>(desc->bits, desc->codebook, prm, L.grid, s);
     if (peer) return launch_gemv_epi<2>(desc->bits, desc->codebook, prm, L.grid, s);
     return launch_gemv_epi<0>(desc->bits, desc->codebook, prm, L.grid, s);
+}
+
+extern "C" int exl3_gemv_prologue_workspace(const exl3_gemv_desc* desc, size_t* xs_bytes)
+{
+    exl3::GemvLaunch L;
+    if (int e = exl3::plan_gemv(desc, &L)) return e;
+    if (xs_bytes) *xs_bytes = prologue_bytes(desc, L);
+    return EXL3_OK;
+}
+
+extern "C" int exl3_gemv_rot(const exl3_gemv_desc* desc, const void* x, int x_dtype, const void* suh,
+                             const uint32_t* const* trellis, const void* svh, void* y, float* partials,
+                             uint32_t* counters, void* xs, size_t xs_bytes, void* stream)
+{
+    const GemvPrologue pro{exl3::kProRot, x, x_dtype, suh, xs, xs_bytes};
+    return gemv_common(desc, nullptr, trellis, svh, y, partials, counters, nullptr, nullptr, 0, &pro, stream);
+}
+
+extern "C" int exl3_gemv_swiglu(const exl3_gemv_desc* desc, const void* gu, int gu_dtype, const void* suh,
+                                const uint32_t* const* trellis, const void* svh, void* y, float* partials,
+                                uint32_t* counters, void* xs, size_t xs_bytes, void* stream)
+{
+    if (!desc) return EXL3_E_NULL;
+    if (desc->n_members != 1) return EXL3_E_SHAPE;
+    const GemvPrologue pro{exl3::kProSwiglu, gu, gu_dtype, suh, xs, xs_bytes};
+    return gemv_common(desc, nullptr, trellis, svh, y, partials, counters, nullptr, nullptr, 0, &pro, stream);
+}
+
+extern "C" int exl3_gemv_swiglu_peer(const exl3_gemv_desc* desc, const void* gu, int gu_dtype, const void* suh,
+                                     const uint32_t* const* trellis, const void* svh, float* partials,
+                                     uint32_t* counters, void* xs, size_t xs_bytes, const exl3_peer_group* g,
+                                     int slot, void* stream)
+{
+    if (!desc || !g) return EXL3_E_NULL;
+    if (desc->n_members != 1) return EXL3_E_SHAPE;
+    const GemvPrologue pro{exl3::kProSwiglu, gu, gu_dtype, suh, xs, xs_bytes};
+    return gemv_common(desc, nullptr, trellis, svh, nullptr, partials, counters, nullptr, g, slot, &pro, stream);
 }
 
 // ---------------------------------------------------------------------------------------- no-alloc
@@ -307,7 +379,7 @@ extern "C" int exl3_gemv_noalloc(const exl3_gemv_desc* desc, const void* xh, con
 extern "C" int exl3_gemv(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis, const void* svh,
                          void* y, float* partials, uint32_t* counters, void* stream)
 {
-    return gemv_common(desc, xh, trellis, svh, y, partials, counters, nullptr, nullptr, 0, stream);
+    return gemv_common(desc, xh, trellis, svh, y, partials, counters, nullptr, nullptr, 0, nullptr, stream);
 }
 
 extern "C" int exl3_gemv_qkv_post(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
@@ -321,7 +393,7 @@ extern "C" int exl3_gemv_qkv_post(const exl3_gemv_desc* desc, const void* xh, co
     if (desc->n_members != 3 || post->hq < 1 || post->hkv < 1 || post->max_len < 1 || desc->n[0] != post->hq * 128 ||
         desc->n[1] != post->hkv * 128 || desc->n[2] != post->hkv * 128)
         return EXL3_E_SHAPE;
-    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, post, nullptr, 0, stream);
+    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, post, nullptr, 0, nullptr, stream);
 }
 
 extern "C" int exl3_gemv_peer(const exl3_gemv_desc* desc, const void* xh, const uint32_t* const* trellis,
@@ -329,5 +401,5 @@ extern "C" int exl3_gemv_peer(const exl3_gemv_desc* desc, const void* xh, const 
                               void* stream)
 {
     if (!desc || !g) return EXL3_E_NULL;
-    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, nullptr, g, slot, stream);
+    return gemv_common(desc, xh, trellis, svh, nullptr, partials, counters, nullptr, g, slot, nullptr, stream);
 }

@@ -59,7 +59,18 @@ struct GemvParams {
     int ll_world;            // > 0: rows go as LL words into ll[0..ll_world) (exl3_gemv_peer; no y)
     uint64_t* ll[8];         // inbox (slot, this rank) of every rank of the group
     const uint32_t* epoch;   // own flag block's "last completed" epoch word
+    // input prologue (PRO > 0): xh is not given but computed by each CTA for the k it reads, into its
+    // own region of xs (laid out as xh: (nm, rows, k) fp16, xs_stride halves per CTA)
+    const void* src;         // PRO 1: x (rows, k); PRO 2: gu (rows, 2k) = [gate | up]
+    int src_dtype;           // EXL3_F16 / EXL3_BF16 / EXL3_F32
+    const __half* suh;       // (nm, k) fp16 input signs
+    __half* xs;
+    long long xs_stride;
 };
+
+// Input prologue kinds: 0 = xh given; 1 = rotation of x (kernels.rot, kernels.py:451-458); 2 = SwiGLU
+// of [gate | up] then the rotation (kernels.swiglu_rot, kernels.py:476-483).
+enum : int { kProNone = 0, kProRot = 1, kProSwiglu = 2 };
 
 constexpr int kRedStride = 8 * 128;   // floats per warp partial (8 rows x 128 columns)
 
@@ -151,6 +162,69 @@ __device__ __forceinline__ void fwht128_rows(float (&v)[4], int lane)
     }
 }
 
+__device__ __forceinline__ float src_at(const void* src, int dtype, size_t i)
+{
+    if (dtype == EXL3_F16) return __half2float(static_cast<const __half*>(src)[i]);
+    if (dtype == EXL3_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+    return static_cast<const float*>(src)[i];
+}
+
+// Input prologue: this CTA's rotated inputs for the 128-column k blocks [kb0, kb1) of every member and
+// row, written into its xs region in the layout of xh. One warp per (member, row, block), with the
+// arithmetic of exl3_rot / exl3_swiglu_rot (exl3_rot.cu), so the values are bit-identical to theirs.
+template <int PRO, int NCW>
+__device__ __forceinline__ void gemv_prologue(const GemvParams& p, __half* xs, int kb0, int kb1, int lane, int cw)
+{
+    const int nkb = kb1 - kb0, k = p.k;
+    const int tasks = p.nm * p.rows * nkb;
+    // A warp takes up to kBatch of its tasks at a time and issues all their loads before any math, so
+    // their L2 round trips overlap instead of following one another.
+    constexpr int kBatch = 4;
+    constexpr int NV = PRO == kProSwiglu ? 2 : 1;                 // source values per element
+    for (int t0 = cw; t0 < tasks; t0 += kBatch * NCW) {
+        float in[kBatch][NV][4], sg[kBatch][4];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int t = t0 + b * NCW;
+            if (t >= tasks) break;
+            const int kb = kb0 + t % nkb, mr = t / nkb, r = mr % p.rows, m = mr / p.rows;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = kb * 128 + lane + 32 * i;
+                if constexpr (PRO == kProRot) {
+                    in[b][0][i] = src_at(p.src, p.src_dtype, (size_t)r * k + c);
+                } else {
+                    in[b][0][i] = src_at(p.src, p.src_dtype, (size_t)r * 2 * k + c);
+                    in[b][NV - 1][i] = src_at(p.src, p.src_dtype, (size_t)r * 2 * k + k + c);
+                }
+                sg[b][i] = __half2float(p.suh[(size_t)m * k + c]);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int t = t0 + b * NCW;
+            if (t >= tasks) break;
+            const int kb = kb0 + t % nkb, mr = t / nkb, r = mr % p.rows, m = mr / p.rows;
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float xv;
+                if constexpr (PRO == kProRot) {
+                    xv = in[b][0][i];
+                } else {
+                    const float gv = in[b][0][i], uv = in[b][NV - 1][i];
+                    xv = gv / (1.0f + expf(-gv)) * uv;
+                }
+                v[i] = xv * sg[b][i];
+            }
+            fwht128_rows(v, lane);
+            __half* o = xs + ((size_t)m * p.rows + r) * k + kb * 128;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[lane + 32 * i] = __float2half_rn(v[i] * kHadScale);
+        }
+    }
+}
+
 template <typename OT>
 __device__ __forceinline__ void finish_row(float (&v)[4], int lane, const float (&sv)[4], OT* yrow)
 {
@@ -221,7 +295,16 @@ __device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const float 
 // The GEMV of one CTA: CTA c of the G CTAs that share the U granules of units starting at unit ubase
 // (the whole launch, or one member's segment of a mixed-bitrate launch); coff is the launch-wide index
 // of the segment's first CTA (its split-k partials).
-template <int K, int CB, int NCW, int EPI>
+// Two xh values: through the read-only path when xh is an input, through L2 when the CTA itself wrote
+// them in its prologue (the non-coherent path may not see writes made during the kernel).
+template <int PRO>
+__device__ __forceinline__ uint32_t ld_x(const __half* p)
+{
+    if constexpr (PRO == kProNone) return __ldg(reinterpret_cast<const unsigned int*>(p));
+    else return __ldcg(reinterpret_cast<const unsigned int*>(p));
+}
+
+template <int K, int CB, int NCW, int EPI, int PRO = kProNone>
 __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, const int c, const int G, const int coff,
                                           const int ubase, const unsigned U)
 {
@@ -292,6 +375,24 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
     pdl_wait();
     int cslot = 0;                                            // ring slot of the unit being decoded
 
+    // Input prologue: the rotated inputs of the k blocks this CTA's units read, into its own xs region
+    // (redundant across CTAs that read the same k, which costs less than a separate launch)
+    __half* xs = nullptr;
+    if constexpr (PRO != kProNone) {
+        xs = p.xs + (size_t)(coff + c) * p.xs_stride;
+        const int KB = p.k / 128;
+        const int lo = u0 - b_first * KT, hi = u1 - b_last * KT;          // k-slices [lo, KT) .. [0, hi)
+        if (b_first == b_last) {
+            gemv_prologue<PRO, NCW>(p, xs, lo / 8, (hi + 7) / 8, lane, cw);
+        } else if (b_last == b_first + 1 && hi < lo) {
+            gemv_prologue<PRO, NCW>(p, xs, 0, (hi + 7) / 8, lane, cw);
+            gemv_prologue<PRO, NCW>(p, xs, lo / 8, KB, lane, cw);
+        } else {
+            gemv_prologue<PRO, NCW>(p, xs, 0, KB, lane, cw);
+        }
+        __syncthreads();                                      // xs written by the CTA's warps
+    }
+
     const int g = lane >> 2, q = lane & 3;
     const LaneWindow<K> lw(lane);
     const HashRegs hr = hash_regs<CB>();
@@ -299,7 +400,7 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
 
     for (int b = b_first; b <= b_last; ++b) {
         const int m = (p.nm > 1 && b >= p.blk_off[1]) ? ((p.nm > 2 && b >= p.blk_off[2]) ? 2 : 1) : 0;
-        const __half* xrow = p.xh + ((size_t)m * rows + g) * p.k;
+        const __half* xrow = (PRO != kProNone ? xs : p.xh) + ((size_t)m * rows + g) * p.k;
         const int sa = max(u0, b * KT) - u0;
         const int se = min(u1, (b + 1) * KT) - u0;
 
@@ -314,15 +415,15 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
         const __half* xp = xrow + (kt_base + i) * 16 + 2 * q;
         uint32_t x0n = 0, x1n = 0;
         if (i < se && xlane) {
-            x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
-            x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
+            x0n = ld_x<PRO>(xp);
+            x1n = ld_x<PRO>(xp + 8);
         }
         for (; i < se; i += NCW) {
             const uint32_t x0 = x0n, x1 = x1n;
             xp += NCW * 16;
             if (i + NCW < se && xlane) {
-                x0n = __ldg(reinterpret_cast<const unsigned int*>(xp));
-                x1n = __ldg(reinterpret_cast<const unsigned int*>(xp + 8));
+                x0n = ld_x<PRO>(xp);
+                x1n = ld_x<PRO>(xp + 8);
             }
             // x duplicated across each k pair: (x[2q], x[2q]), (x[2q+8], ..), (x[2q+1], ..), (x[2q+9], ..)
             const uint32_t be0 = prmt(x0, x0, 0x1010), be1 = prmt(x1, x1, 0x1010);
@@ -460,11 +561,11 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
     }
 }
 
-template <int K, int CB, int NCW, int EPI>
+template <int K, int CB, int NCW, int EPI, int PRO>
 __global__ void __launch_bounds__(32 * NCW, 1) gemv_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    gemv_body<K, CB, NCW, EPI>(p, smem, blockIdx.x, gridDim.x, 0, 0, (unsigned)(p.units / p.gran));
+    gemv_body<K, CB, NCW, EPI, PRO>(p, smem, blockIdx.x, gridDim.x, 0, 0, (unsigned)(p.units / p.gran));
 }
 
 // Members of different bitrates in one launch (e.g. q/k/v quantised at different bpw): member m owns
@@ -512,7 +613,7 @@ inline int gemv_smem_bytes(int bits)
 }
 
 
-template <int K, int CB, int EPI>
+template <int K, int CB, int EPI, int PRO>
 static int launch_gemv_k(const GemvParams& prm, int grid, cudaStream_t s)
 {
     using S = GemvShape<K, kNCW>;
@@ -520,39 +621,39 @@ static int launch_gemv_k(const GemvParams& prm, int grid, cudaStream_t s)
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemv_kernel<K, CB, kNCW, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(gemv_kernel<K, CB, kNCW, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  S::SMEM) != cudaSuccess)
             return EXL3_E_CUDA;
         attr_set[dev] = true;
     }
-    if (int e_ = launch_pdl(gemv_kernel<K, CB, kNCW, EPI>, grid, S::THREADS, S::SMEM, s, prm)) return e_;
+    if (int e_ = launch_pdl(gemv_kernel<K, CB, kNCW, EPI, PRO>, grid, S::THREADS, S::SMEM, s, prm)) return e_;
     return launch_status();
 }
 
-template <int K, int EPI>
+template <int K, int EPI, int PRO>
 static int launch_gemv_cb(int cb, const GemvParams& prm, int grid, cudaStream_t s)
 {
     switch (cb) {
-    case 0: return launch_gemv_k<K, 0, EPI>(prm, grid, s);
-    case 1: return launch_gemv_k<K, 1, EPI>(prm, grid, s);
-    default: return launch_gemv_k<K, 2, EPI>(prm, grid, s);
+    case 0: return launch_gemv_k<K, 0, EPI, PRO>(prm, grid, s);
+    case 1: return launch_gemv_k<K, 1, EPI, PRO>(prm, grid, s);
+    default: return launch_gemv_k<K, 2, EPI, PRO>(prm, grid, s);
     }
 }
 
 // Every K and codebook for one finish kind; instantiated once per kind (exl3_gemv.cu: 0,
 // exl3_gemv_fused.cu: 1 and 2) so the translation units compile in parallel.
-template <int EPI>
+template <int EPI, int PRO = kProNone>
 int launch_gemv_epi(int bits, int cb, const GemvParams& prm, int grid, cudaStream_t s)
 {
     switch (bits) {
-    case 1: return launch_gemv_cb<1, EPI>(cb, prm, grid, s);
-    case 2: return launch_gemv_cb<2, EPI>(cb, prm, grid, s);
-    case 3: return launch_gemv_cb<3, EPI>(cb, prm, grid, s);
-    case 4: return launch_gemv_cb<4, EPI>(cb, prm, grid, s);
-    case 5: return launch_gemv_cb<5, EPI>(cb, prm, grid, s);
-    case 6: return launch_gemv_cb<6, EPI>(cb, prm, grid, s);
-    case 7: return launch_gemv_cb<7, EPI>(cb, prm, grid, s);
-    default: return launch_gemv_cb<8, EPI>(cb, prm, grid, s);
+    case 1: return launch_gemv_cb<1, EPI, PRO>(cb, prm, grid, s);
+    case 2: return launch_gemv_cb<2, EPI, PRO>(cb, prm, grid, s);
+    case 3: return launch_gemv_cb<3, EPI, PRO>(cb, prm, grid, s);
+    case 4: return launch_gemv_cb<4, EPI, PRO>(cb, prm, grid, s);
+    case 5: return launch_gemv_cb<5, EPI, PRO>(cb, prm, grid, s);
+    case 6: return launch_gemv_cb<6, EPI, PRO>(cb, prm, grid, s);
+    case 7: return launch_gemv_cb<7, EPI, PRO>(cb, prm, grid, s);
+    default: return launch_gemv_cb<8, EPI, PRO>(cb, prm, grid, s);
     }
 }
 
@@ -591,5 +692,8 @@ extern template int launch_gemv_seg<1>(int, const GemvParams&, int, int, cudaStr
 extern template int launch_gemv_epi<0>(int, int, const GemvParams&, int, cudaStream_t);
 extern template int launch_gemv_epi<1>(int, int, const GemvParams&, int, cudaStream_t);
 extern template int launch_gemv_epi<2>(int, int, const GemvParams&, int, cudaStream_t);
+extern template int launch_gemv_epi<0, kProRot>(int, int, const GemvParams&, int, cudaStream_t);
+extern template int launch_gemv_epi<0, kProSwiglu>(int, int, const GemvParams&, int, cudaStream_t);
+extern template int launch_gemv_epi<2, kProSwiglu>(int, int, const GemvParams&, int, cudaStream_t);
 
 }  // namespace exl3

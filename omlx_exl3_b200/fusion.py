@@ -8,8 +8,9 @@ can emit the rotations as a by-product instead:
   norm sites   an RMSNorm read only by EXL3 consumers (attention input norm -> q/k/v or
                in_proj_qkv/z, MLP input norm -> gate/up, final norm -> lm_head): kernels.norm_rot writes
                the normalised tensor and the rotated input of every consumer in one launch
-  MLP sites    gate/up sibling group -> SwiGLU -> down_proj: kernels.swiglu_rot turns the gate/up GEMV
-               output straight into down_proj's rotated input
+  MLP sites    gate/up sibling group -> SwiGLU -> down_proj: down_proj's GEMV computes SwiGLU and its
+               own input rotation from the gate/up GEMV output in the same launch
+               (TrellisGemvPlan.swiglu_call)
 
 `fuse_decode(model)` finds the sites and attaches a `FusionSite` to each producer module. The site
 replaces the module's forward through an instance attribute only, so the module keeps its class,
@@ -28,7 +29,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from .kernels import MAX_GEMV_ROWS, norm_rot, swiglu_rot
+from .kernels import MAX_GEMV_ROWS, norm_rot
 from .linear import EXL3Linear
 
 ENABLED = True          # False sends every fused module down its original forward (for A/B timing)
@@ -90,7 +91,8 @@ class NormSite(FusionSite):
 
 
 class MlpSite(FusionSite):
-    """gate/up group -> SwiGLU -> down_proj: the SwiGLU kernel emits down_proj's rotated input."""
+    """gate/up group -> SwiGLU -> down_proj: down_proj's GEMV takes the gate/up output and computes
+    SwiGLU and its input rotation itself (one launch less than swiglu_rot + GEMV, bit-identical)."""
 
     kind = "mlp"
 
@@ -100,8 +102,8 @@ class MlpSite(FusionSite):
 
     def fused(self, x: torch.Tensor) -> torch.Tensor:
         gu = self.gate_up.gemv(x, torch.float16)                           # (rows, 2 * n): gate | up
-        xh = swiglu_rot(gu, self.down.rot_suh.reshape(-1))
-        y = self.down.gemv_rotated(xh, x.dtype)
+        d = self.down
+        y = d.plan(gu.shape[0], x.dtype).swiglu_call(gu, d.rot_suh, [d.trellis_words])
         return y.view(*x.shape[:-1], y.shape[-1])
 
 

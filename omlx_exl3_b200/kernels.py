@@ -105,6 +105,77 @@ class TrellisGemvPlan:
         return y
 
 
+    def _xs(self) -> torch.Tensor:
+        """Scratch of the input prologue (exl3_gemv_prologue_workspace bytes), made on first use."""
+        xs = self.__dict__.get("_xs_buf")
+        if xs is None:
+            nb = ctypes.c_size_t()
+            check(lib().exl3_gemv_prologue_workspace(self._desc_ref, ctypes.byref(nb)), "exl3_gemv_prologue_workspace")
+            xs = self._xs_buf = torch.empty(max(nb.value // 2, 8), dtype=torch.float16, device=self.device)
+        return xs
+
+    def _check_trellises(self, trellises):
+        assert len(trellises) == self.nsub
+        _need_cuda(*trellises)
+        for t, n, Km in zip(trellises, self.member_ns, self.Ks):
+            if t.numel() * t.element_size() != self.k * n * Km // 8:
+                raise ValueError(f"trellis holds {t.numel() * t.element_size()} bytes, expected "
+                                 f"{self.k * n * Km // 8} for {self.k}x{n} at {Km} bpw")
+        for i in range(3):
+            self._tptr[i] = trellises[i if i < self.nsub else 0].data_ptr()
+
+    def rot_call(self, x: torch.Tensor, suh: torch.Tensor, trellises: list[torch.Tensor],
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        """rot(x, suh) and the GEMV in one launch (exl3_gemv_rot): x (rows, k) fp16/bf16/fp32, suh fp16
+        (n_members, k) -> (rows, n) in out_dtype; bit-identical to plan(rot(x, suh), trellises)."""
+        x = x.reshape(self.rows, self.k)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        if suh.dtype != torch.float16 or not suh.is_contiguous():
+            suh = suh.to(torch.float16).contiguous()
+        if suh.numel() != self.nsub * self.k:
+            raise ValueError(f"suh has {suh.numel()} elements, expected {self.nsub}x{self.k}")
+        _need_cuda(x, suh)
+        self._check_trellises(trellises)
+        xs = self._xs()
+        y = out if out is not None else torch.empty((self.rows, self.n), dtype=self.out_dtype, device=x.device)
+        check(lib().exl3_gemv_rot(self._desc_ref, x.data_ptr(), dtype_code(x.dtype), suh.data_ptr(), self._tptr_arg,
+                                  self.svh.data_ptr(), y.data_ptr(), self.partials.data_ptr(),
+                                  self.counters.data_ptr(), xs.data_ptr(), xs.numel() * 2, stream_ptr(x.device)),
+              "exl3_gemv_rot")
+        return y
+
+    def swiglu_call(self, gu: torch.Tensor, suh: torch.Tensor, trellises: list[torch.Tensor], peers=None,
+                    slot: int = 0, out: torch.Tensor | None = None) -> torch.Tensor | None:
+        """swiglu_rot(gu, suh) and the GEMV in one launch for a one-member plan (k = the MLP width):
+        gu (rows, 2k) = [gate | up] fp16/bf16. Returns (rows, n) in out_dtype (exl3_gemv_swiglu), or,
+        with peers (comm.PeerGroup), pushes the rows into inbox (slot, rank) of every rank and returns
+        None (exl3_gemv_swiglu_peer)."""
+        assert self.nsub == 1
+        if gu.shape != (self.rows, 2 * self.k):
+            raise ValueError(f"gu must be ({self.rows}, {2 * self.k})")
+        if not gu.is_contiguous():
+            gu = gu.contiguous()
+        suh = suh.reshape(-1)
+        if suh.dtype != torch.float16 or not suh.is_contiguous():
+            suh = suh.to(torch.float16).contiguous()
+        _need_cuda(gu, suh)
+        self._check_trellises(trellises)
+        xs = self._xs()
+        if peers is not None:
+            check(lib().exl3_gemv_swiglu_peer(self._desc_ref, gu.data_ptr(), dtype_code(gu.dtype), suh.data_ptr(),
+                                              self._tptr_arg, self.svh.data_ptr(), self.partials.data_ptr(),
+                                              self.counters.data_ptr(), xs.data_ptr(), xs.numel() * 2,
+                                              ctypes.byref(peers.desc), slot, stream_ptr(gu.device)),
+                  "exl3_gemv_swiglu_peer")
+            return None
+        y = out if out is not None else torch.empty((self.rows, self.n), dtype=self.out_dtype, device=gu.device)
+        check(lib().exl3_gemv_swiglu(self._desc_ref, gu.data_ptr(), dtype_code(gu.dtype), suh.data_ptr(),
+                                     self._tptr_arg, self.svh.data_ptr(), y.data_ptr(), self.partials.data_ptr(),
+                                     self.counters.data_ptr(), xs.data_ptr(), xs.numel() * 2, stream_ptr(gu.device)),
+              "exl3_gemv_swiglu")
+        return y
+
     def qkv_post(self, xh: torch.Tensor, trellises: list[torch.Tensor], q_norm_w: torch.Tensor,
                  k_norm_w: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor,
                  k_cache: torch.Tensor, v_cache: torch.Tensor, q_out: torch.Tensor | None = None) -> torch.Tensor:

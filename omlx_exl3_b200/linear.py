@@ -11,9 +11,9 @@ The product it computes, for an input x of any leading shape, is
     y = H(H(x * suh) @ W) * svh  (+ bias)          H: 128-point Walsh-Hadamard blocks scaled by 1/sqrt(128)
 
 where W is the k x n matrix the trellis decodes to. Up to MAX_GEMV_ROWS rows (batch decode, speculative
-verify) the input rotation is one kernel (skipped when a fused producer has already written it, see
-`prime`) and the rest is one GEMV launch that decodes the trellis on the fly. Larger inputs take the
-prefill path (prefill.py).
+verify) it is one GEMV launch that rotates its own input, decodes the trellis on the fly and applies
+the output rotation (or, when a fused producer has already written the rotated input, see `prime`, the
+GEMV alone). Larger inputs take the prefill path (prefill.py).
 
 `EXL3SiblingGroup` ties 2-3 linears that read the same input (q/k/v, gate/up, in_proj_qkv/z) into a
 single GEMV launch over their separate trellis buffers.
@@ -30,7 +30,7 @@ import torch
 from torch import nn
 
 from . import prefill
-from .kernels import MAX_GEMV_ROWS, TrellisGemvPlan, rot
+from .kernels import MAX_GEMV_ROWS, TrellisGemvPlan
 
 PREFILL_COL_CHUNK = 16384          # output columns decoded per chunk on the unfused prefill path
 
@@ -155,10 +155,11 @@ class EXL3Linear(nn.Module):
                                        rt.suh, rt.svh)
         else:
             xh = self._take_primed(x)
-            if xh is None:
-                xh = rot(x2, self.rot_suh)
             gemv_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
-            y = self.gemv_rotated(xh, gemv_dtype)
+            if xh is not None:
+                y = self.gemv_rotated(xh, gemv_dtype)
+            else:            # one launch: the GEMV rotates its own input (exl3_gemv_rot)
+                y = self.plan(x2.shape[0], gemv_dtype).rot_call(x2, rt.suh, [rt.words])
         y = y.to(x.dtype)
         if "bias" in self:
             y = y + self.bias.to(y.dtype)
@@ -214,8 +215,10 @@ class EXL3SiblingGroup:
         """One launch for all members: (rows, sum(ns)) in out_dtype, members side by side."""
         handed, self._primed = self._primed, None
         x2 = x.reshape(-1, self.k)
-        xh = handed[1] if handed is not None and handed[0] is x else rot(x2, self.suh)
-        return self.plan(x2.shape[0], out_dtype)(xh, self.trs)
+        plan = self.plan(x2.shape[0], out_dtype)
+        if handed is not None and handed[0] is x:
+            return plan(handed[1], self.trs)
+        return plan.rot_call(x2, self.suh, self.trs)         # one launch: the GEMV rotates its input
 
     def member_output(self, x: torch.Tensor, idx: int) -> torch.Tensor:
         """Output of member idx for input x. A group result is handed to each member once: tensors are

@@ -26,6 +26,13 @@ from .kernels import (MAX_GEMV_ROWS, TrellisGemvPlan, add_norm_rot, argmax, attn
                       rot, swiglu_rot)
 from .linear import EXL3Linear
 
+# Up to this MLP width (per rank) the decode step's down_proj GEMV computes SwiGLU and its input rotation
+# itself (TrellisGemvPlan.swiglu_call), one launch less. Every CTA rotates the k blocks its units read, so
+# the work is repeated once per 128-column block of the output: measured on B200 (graphs of 50 calls,
+# 6 bpw, 5120 outputs, 1 row) 9.9 -> 9.2 us at k = 2176 and 13.9 -> 13.1 at 4352, but 32.2 -> 33.7 at
+# 17408, where the separate SwiGLU kernel stays.
+FUSED_SWIGLU_MAX_K = 4352
+
 
 @dataclass
 class ModelConfig:
@@ -447,7 +454,17 @@ class Qwen3EXL3(nn.Module):
             gu = gu_outs[0] if len(gu_outs) == 1 else torch.cat(
                 [_cols(gu_outs, lp.gu_at[0]), _cols(gu_outs, lp.gu_at[1])], dim=1)
             down = layer.mlp.down_proj
-            pending = row_parallel(down, swiglu_rot(gu, down.rot_suh.reshape(-1)))
+            if down.in_features <= FUSED_SWIGLU_MAX_K:
+                # down_proj's GEMV computes SwiGLU and its own input rotation from gu in the same launch
+                dplan = down.plan(rows, dt)
+                if peers is None:
+                    pending = self.tp.all_reduce(dplan.swiglu_call(gu, down.rot_suh, [down.trellis_words]))
+                else:
+                    dplan.swiglu_call(gu, down.rot_suh, [down.trellis_words], peers=peers, slot=slot)
+                    pending = slot
+                    slot ^= 1
+            else:
+                pending = row_parallel(down, swiglu_rot(gu, down.rot_suh.reshape(-1)))
         w_out = self.model.norm.weight
         head = self.__dict__["_head_targets"]
         if head is None:

@@ -107,6 +107,41 @@ def test_gemv_peer_feeds_ar(cuda, dtype, rows):
         B.close()
 
 
+@pytest.mark.parametrize("rows", [1, 4])
+def test_gemv_swiglu_peer_feeds_ar(cuda, rows):
+    """exl3_gemv_swiglu_peer (the tensor-parallel down_proj: SwiGLU + rotation + GEMV + push in one
+    launch) as rank 0's producer: the all-reduce sees exactly swiglu_rot + the plain GEMV's output."""
+    from omlx_exl3_b200 import kernels
+    from omlx_exl3_b200.kernels import TrellisGemvPlan
+    k_in, k, K, dtype = 2176, 2560, 6, torch.bfloat16
+    g = torch.Generator(device=cuda)
+    g.manual_seed(rows + 11)
+    tr = torch.randint(-2 ** 31, 2 ** 31 - 1, (k_in * k * K // 32,), dtype=torch.int32, device=cuda, generator=g)
+    svh = (torch.randint(0, 2, (k,), device=cuda, generator=g).half() * 2 - 1) * 0.03
+    dsuh = (torch.randint(0, 2, (k_in,), device=cuda, generator=g) * 2 - 1).half()
+    plan = TrellisGemvPlan(k_in, [k], K, 0, svh, rows, dtype)
+    A, B = _emulated_pair(cuda)
+    try:
+        w = (1 + 0.1 * torch.randn(k, device=cuda, generator=g)).to(dtype)
+        suh = (0.5 * torch.randn((1, k), device=cuda, generator=g)).half()
+        for call, slot in enumerate((0, 1)):
+            gu = (2 * torch.randn((rows, 2 * k_in), device=cuda, generator=g)).half()
+            x = (3 * torch.randn((rows, k), device=cuda, generator=g)).to(dtype)
+            d1 = (2 * torch.randn((rows, k), device=cuda, generator=g)).to(dtype)
+            d0 = plan(kernels.swiglu_rot(gu, dsuh), [tr])
+            plan.swiglu_call(gu, dsuh, [tr], peers=A, slot=slot)
+            B.put(slot, d1)
+            h, xn, xh = A.ar_add_norm_rot(slot, x, w, 1e-6, suh)
+            B.ar_add_norm_rot(slot, x, w, 1e-6, suh)
+            eh, exn, _ = _expected(x, [d0, d1], w, 1e-6, suh)
+            torch.cuda.synchronize()
+            _check(h, xn, xh, eh, exn, suh)
+        assert A.status() == 0 and int(plan.counters.abs().sum().item()) == 0
+    finally:
+        A.close()
+        B.close()
+
+
 def test_ar_wait_times_out_with_status(cuda):
     """A source rank that never pushes: the bounded wait gives up after ~2 s, sets status bit 4 and
     returns; the context stays usable."""

@@ -194,3 +194,61 @@ def test_gemv_rejects_bad_input(cuda):
     with pytest.raises(ValueError):
         plan(torch.zeros((1, 2, 1024), dtype=torch.float16, device=cuda),
              [torch.zeros(1024 * 256 * 4 // 32, dtype=torch.int32, device=cuda)])
+
+
+# ---------------------------------------------------------------------------------------------- fused input
+# The GEMV that computes its own rotated input (exl3_gemv_rot / exl3_gemv_swiglu): every CTA rotates
+# the k blocks its units read with the arithmetic of exl3_rot / exl3_swiglu_rot, so the result must
+# equal the two-launch path bit for bit. Forced small grids make CTAs span one, two (disjoint k
+# ranges) and several blocks, which exercises every prologue range.
+
+@pytest.mark.parametrize("xdtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows", [1, 3, 8])
+@pytest.mark.parametrize("ns,K", [([1024], 6), ([512, 256, 256], 4), ([384, 128], 5)])
+def test_gemv_rot_equals_rot_then_gemv(cuda, xdtype, rows, ns, K):
+    from omlx_exl3_b200 import kernels
+    from omlx_exl3_b200.kernels import TrellisGemvPlan
+    g = torch.Generator(device=cuda)
+    g.manual_seed(rows * 7 + K)
+    k = 2048
+    trs = [_t(O.random_trellis(k, n, K, 50 + i), cuda) for i, n in enumerate(ns)]
+    svh = (torch.randn(sum(ns), device=cuda, generator=g) * 0.02).half()
+    suh = (torch.randint(0, 2, (len(ns), k), device=cuda, generator=g) * 2 - 1).half()
+    x = torch.randn((rows, k), device=cuda, generator=g).to(xdtype)
+    for grid in (0, 3, 7, 50):
+        plan = TrellisGemvPlan(k, ns, K, 0, svh, rows, torch.float16, grid=grid)
+        ref = plan(kernels.rot(x, suh), trs).clone()
+        got = plan.rot_call(x, suh, trs)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), grid
+        assert int(plan.counters.abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("gdtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("rows", [1, 4, 8])
+def test_gemv_swiglu_equals_swiglu_rot_then_gemv(cuda, gdtype, rows):
+    from omlx_exl3_b200 import kernels
+    from omlx_exl3_b200.kernels import TrellisGemvPlan
+    g = torch.Generator(device=cuda)
+    g.manual_seed(rows)
+    k, n, K = 4352, 1024, 6                   # down_proj-like: k = the MLP width
+    tr = _t(O.random_trellis(k, n, K, 60), cuda)
+    svh = (torch.randn(n, device=cuda, generator=g) * 0.02).half()
+    suh = (torch.randint(0, 2, (k,), device=cuda, generator=g) * 2 - 1).half()
+    gu = (2 * torch.randn((rows, 2 * k), device=cuda, generator=g)).to(gdtype)
+    for grid in (0, 5, 33):
+        plan = TrellisGemvPlan(k, [n], K, 0, svh, rows, torch.bfloat16, grid=grid)
+        ref = plan(kernels.swiglu_rot(gu, suh), [tr]).clone()
+        got = plan.swiglu_call(gu, suh, [tr])
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), grid
+
+
+def test_gemv_prologue_rejects_bad_input(cuda):
+    from omlx_exl3_b200.kernels import TrellisGemvPlan
+    svh = torch.ones(256, dtype=torch.float16, device=cuda)
+    tr = torch.zeros(1040 * 256 * 4 // 32, dtype=torch.int32, device=cuda)
+    plan = TrellisGemvPlan(1040, [256], 4, 0, svh, 1)            # k % 128 != 0: no in-kernel rotation
+    with pytest.raises(ValueError):
+        plan.rot_call(torch.zeros((1, 1040), dtype=torch.float16, device=cuda),
+                      torch.ones((1, 1040), dtype=torch.float16, device=cuda), [tr])
