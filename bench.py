@@ -354,6 +354,63 @@ def run_decode(args, torch, dist, rank, world, dev, layers=64, rows=1, head=True
             "gemv": gemv, "clocks": clk}
 
 
+def run_timeline(args, torch, dist, rank, world, dev, layers=8, rows=1):
+    """Per-kernel critical-path breakdown of the graph-replayed decode step at this tensor-parallel size.
+
+    CUPTI kernel records (torch.profiler) of the last of three replays are sorted by start; each kernel is
+    charged the time by which it moves the step's end (its end minus the latest end before it), so the
+    increments sum to the step's span and overlapped work (a dependent launch's prologue, the weight
+    prefetch) costs nothing. Rank 0 prints one JSON line: per kernel kind launches per layer, increment
+    per layer and mean duration."""
+    import collections
+    from torch.profiler import ProfilerActivity, profile
+    from omlx_exl3_b200.decode import DecodeRunner
+
+    model = build_model(torch, layers, rank, world, dev)
+    cache = kv_cache_for(model, 1, dev)
+    runner = DecodeRunner(model, cache, rows=rows, use_graph=True, check_every=0)
+    for _ in range(args.warmup):
+        runner.step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        runner.step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us_layer = e0.elapsed_time(e1) * 1000.0 / args.steps / layers
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(3):
+            runner.step()
+        torch.cuda.synchronize(dev)
+    runner.check()
+    ks = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                if e.device_type.name == "CUDA")
+    ks = ks[-(len(ks) // 3):]
+    inc, dur, cnt = collections.defaultdict(float), collections.defaultdict(float), collections.Counter()
+    prev_end = ks[0][0]
+    for st, en, name in ks:
+        kind = name.split("(")[0].replace("void ", "")
+        inc[kind] += max(0.0, en - prev_end)
+        dur[kind] += en - st
+        cnt[kind] += 1
+        prev_end = max(prev_end, en)
+    runner.release()
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    model.close_peers()
+    if rank != 0:
+        return None
+    kinds = sorted(inc, key=lambda k: -inc[k])
+    return {"timeline": {"tp": world, "layers": layers, "rows": rows, "us_per_layer_graph": round(us_layer, 2),
+                         "profiled_step_us": round(ks[-1][1] - ks[0][0], 1),
+                         "kernels": [{"kernel": k, "launches_per_layer": round(cnt[k] / layers, 3),
+                                      "increment_us_per_layer": round(inc[k] / layers, 2),
+                                      "us_per_launch": round(dur[k] / cnt[k], 2)} for k in kinds]}}
+
+
 def run_tp_parity(torch, dist, rank, world, dev, layers=2):
     """Logits of one decode step of a `layers`-layer model of the config-5 shapes, tensor-parallel over
     the group (fused peer all-reduce, logits gathered) against the same model unsharded on this rank.
@@ -544,9 +601,12 @@ def run_config1(args, torch, dev, peaks):
 # ------------------------------------------------------------------------------------------ prefill
 
 def run_prefill(args, torch, dev, peaks):
-    """prefill GEMM at 6 bpw, M in {512, 4096} x (5120->17408, 17408->5120), bf16 out,
-    the shipped default path and the decode-once + library GEMM path side by side; TFLOP/s counts
-    2*M*k*n; each call timed alone, so the fraction is of the burst bf16 peak."""
+    """prefill GEMM at 6 bpw, M in {512, 4096} x (5120->17408, 17408->5120), bf16 out.
+    Side by side: the fused kernel (trellis decoded in shared memory), decode-once + this package's
+    tcgen05 GEMM on the decoded weights, the same GEMM alone (its own tensor-core rate), and decode-once +
+    the library GEMM + had_svh (cuBLAS, a comparison only: never shipped). `default` is what
+    prefill.linear_prefill runs. TFLOP/s counts 2*M*k*n; each call is timed alone, so the fraction is of the
+    burst bf16 peak."""
     from omlx_exl3_b200 import kernels
     from omlx_exl3_b200.prefill import use_fused
 
@@ -558,10 +618,10 @@ def run_prefill(args, torch, dev, peaks):
         K = 6
         tr = torch.randint(-2 ** 31, 2 ** 31 - 1, (k * n * K // 32,), dtype=torch.int32, device=dev, generator=gen)
         svh = (torch.randint(0, 2, (n,), device=dev, generator=gen).to(torch.float16) * 2 - 1)
+        wt = torch.empty((n, k), dtype=torch.float16, device=dev)
         for M in (512, 4096):
             xh = torch.randn((M, k), device=dev, generator=gen).to(torch.float16)
             y = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
-            wt = torch.empty((n, k), dtype=torch.float16, device=dev)
             yh = torch.empty((M, n), dtype=torch.float16, device=dev)
 
             def fused():
@@ -569,12 +629,20 @@ def run_prefill(args, torch, dev, peaks):
 
             def decode_once():
                 kernels.decode_wt(tr, k, n, K, 0, out=wt)
+                kernels.gemm_wt(xh, wt, svh, out=y)
+
+            def gemm_alone():
+                kernels.gemm_wt(xh, wt, svh, out=y)
+
+            def decode_once_cublas():
+                kernels.decode_wt(tr, k, n, K, 0, out=wt)
                 torch.matmul(xh, wt.t(), out=yh)
                 kernels.had_svh(yh, svh, torch.bfloat16)
 
             res = {"M": M, "k": k, "n": n, "bits": K,
-                   "default": "fused_tcgen05" if use_fused(M, n) else "decode_once_gemm"}
-            for name, fn in (("fused_tcgen05", fused), ("decode_once_gemm", decode_once)):
+                   "default": "fused_tcgen05" if use_fused(M, n) else "decode_once_tcgen05"}
+            for name, fn in (("fused_tcgen05", fused), ("decode_once_tcgen05", decode_once),
+                             ("gemm_wt_alone", gemm_alone), ("decode_once_cublas", decode_once_cublas)):
                 for _ in range(3):
                     fn()
                 torch.cuda.synchronize(dev)
@@ -589,8 +657,8 @@ def run_prefill(args, torch, dev, peaks):
                 tf = 2.0 * M * k * n / (ms * 1e-3) / 1e12
                 res[name] = {"us": round(ms * 1000, 1), "TFLOPs": round(tf, 1), "frac": round(tf / tf_peak, 4)}
             cases.append(res)
-            del xh, y, wt, yh
-        del tr
+            del xh, y, yh
+        del tr, wt
     torch.cuda.empty_cache()
     return {"peak_TFLOPs": tf_peak, "peak_kind": f"{peaks['kind']} bf16 burst (each call timed alone; fp16 has the "
                                                   "same rate)", "status": kernels.gemm_status(dev), "cases": cases}
@@ -753,7 +821,7 @@ def run_ours(args, torch, dist, rank, world, dev):
     if gemv:
         roof.update(achieved=gemv["achieved_GBps"], frac=round(gemv["achieved_GBps"] / peaks["hbm"], 4),
                     # DRAM (read + write) / algorithmic bytes of one ncu capture of the GEMV, per launch
-                    traffic=int(gemv["bytes_per_launch"] * 1.0057), traffic_unit="bytes per launch",
+                    traffic=int(gemv["bytes_per_launch"] * 1.003), traffic_unit="bytes per launch",
                     launches=gemv["launches"], us_per_launch=gemv["us_per_launch"])
     roof["step_GBps_per_gpu"] = dec["step_GBps_per_gpu"]
     roof["step_frac"] = round(dec["step_GBps_per_gpu"] / peaks["hbm"], 4)
@@ -795,6 +863,9 @@ def main():
     ap.add_argument("--decode-layers", type=int, default=64)
     ap.add_argument("--decode-only", action="store_true", help="only the headline decode measurement")
     ap.add_argument("--tp-parity-only", action="store_true", help="only the tensor-parallel logit check")
+    ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill GEMM measurement")
+    ap.add_argument("--timeline", action="store_true",
+                    help="per-kernel critical-path breakdown of the decode step (--decode-layers layers)")
     ap.add_argument("--sweep-case", default=None,
                     help="k,n,K,rows: time one GEMV configuration alone and exit (small ncu captures)")
     args = ap.parse_args()
@@ -823,6 +894,14 @@ def main():
             k, n, K, rows = (int(v) for v in args.sweep_case.split(","))
             SWEEP_SHAPES, SWEEP_BITS, SWEEP_ROWS = [(k, n)], [K], [rows]
             print(json.dumps({"sweep_case": run_sweep(args, torch, dev, load_peaks())}), flush=True)
+            return
+        if args.prefill_only:
+            print(json.dumps({"prefill_gemm": run_prefill(args, torch, dev, load_peaks())}), flush=True)
+            return
+        if args.timeline:
+            res = run_timeline(args, torch, dist, rank, world, dev, layers=args.decode_layers)
+            if res is not None:
+                print(json.dumps(res), flush=True)
             return
         if args.tp_parity_only:
             res = run_tp_parity(torch, dist, rank, world, dev)

@@ -173,6 +173,23 @@ EXL3_API int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* trel
                        const void* svh, void* y, int out_dtype, uint32_t* status, void* stream);
 
 /*
+ * Prefill GEMM on weights already decoded by exl3_decode_wt (tcgen05 pairs of SMs, both operands by TMA):
+ *   y[:, 0:n] = out_dtype( had128(xh @ wt^T) / sqrt(128) * svh ),  xh fp16 (M, k), wt fp16 (n, k) row-major
+ *   (the decode_wt layout: row j = output column j), y rows ldy elements apart (ldy >= n), so a column
+ *   chunk of a wider output is written in place.
+ * Replaces: the matmul, _had128 and * svh of EXL3Linear._prefill (src/omlx/exl3/linear.py:101-105) for one
+ * chunk of decode_wt columns. k % 64 == 0, n % 128 == 0, any M >= 1; out_dtype EXL3_F16, EXL3_BF16 or
+ * EXL3_F32; xh, wt and y 16-byte aligned, ldy * element size a multiple of 16. `status` as for exl3_gemm.
+ * workspace (256-byte aligned) of exl3_gemm_wt_workspace bytes lets the call split k over several work
+ * units for shapes with few output tiles; its first bytes are arrival counters that must be zero before
+ * the first call (every completed call leaves them zero). A null or smaller workspace runs unsplit.
+ * Calls that share a workspace must not overlap.
+ */
+EXL3_API int exl3_gemm_wt_workspace(int M, int k, int n, size_t* bytes);
+EXL3_API int exl3_gemm_wt(const void* xh, int M, int k, int n, const void* wt, const void* svh, void* y, int ldy,
+                          int out_dtype, void* workspace, size_t workspace_bytes, uint32_t* status, void* stream);
+
+/*
  * Output rotation: out[r, :] = out_dtype(had128(y[r, :]) / sqrt(128) * svh), y (rows, n) of y_dtype.
  * Replaces: the prefill tail `_had128(y) * self._svh` (src/omlx/exl3/linear.py:105, :31-33).
  * svh: fp16 (n); n % 128 == 0.

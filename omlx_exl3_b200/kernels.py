@@ -453,6 +453,54 @@ def gemm(xh: torch.Tensor, trellis_u32: torch.Tensor, k: int, n: int, K: int, cb
     return y
 
 
+_wt_workspaces: dict = {}
+
+
+def _gemm_wt_workspace(device: torch.device, M: int, k: int, n: int) -> tuple[int, int]:
+    """(pointer, bytes) of this device's k-split workspace for an M x k x n call, grown on demand; new
+    buffers are zeroed (the arrival counters must be zero at rest). (0, 0) when the call runs unsplit."""
+    need = ctypes.c_size_t()
+    check(lib().exl3_gemm_wt_workspace(M, k, n, ctypes.byref(need)), "exl3_gemm_wt_workspace")
+    if need.value == 0:
+        return 0, 0
+    key = torch.device(device)
+    buf = _wt_workspaces.get(key)
+    if buf is None or buf.numel() < need.value:
+        buf = torch.zeros(need.value, dtype=torch.uint8, device=key)
+        _wt_workspaces[key] = buf
+    return buf.data_ptr(), buf.numel()
+
+
+def gemm_wt(xh: torch.Tensor, wt: torch.Tensor, svh: torch.Tensor, out_dtype: torch.dtype = torch.float32,
+            out: torch.Tensor | None = None, split: bool = True) -> torch.Tensor:
+    """Prefill product on decoded weights: out_dtype(had128(xh @ wt^T) / sqrt(128) * svh) for xh fp16 (M, k)
+    and wt fp16 (n, k) as decode_wt returns it (linear.py:101-105). `out` may be a column slice of a wider
+    row-major matrix (unit column stride); the rows are written in place. Needs k % 64 == 0, n % 128 == 0.
+    With `split` the call may cut k into parts summed in a fixed order (a per-device workspace; calls on
+    one device must not run concurrently on several streams). Raises RuntimeError once an earlier launch
+    on this device reported a timed-out wait."""
+    M, k = xh.shape
+    n = wt.shape[0]
+    _need_cuda(xh, wt, svh)
+    if xh.dtype != torch.float16 or wt.dtype != torch.float16:
+        raise TypeError("xh and wt must be fp16")
+    if wt.shape[1] != k:
+        raise ValueError(f"wt is {tuple(wt.shape)}, expected ({n}, {k})")
+    st = _status(xh.device)
+    st.before_launch()
+    xh, wt = xh.contiguous(), wt.contiguous()
+    svh = svh.to(torch.float16).reshape(-1).contiguous()
+    y = out if out is not None else torch.empty((M, n), dtype=out_dtype, device=xh.device)
+    if y.shape != (M, n) or y.stride(1) != 1:
+        raise ValueError("out must be (M, n) with unit column stride")
+    ws, ws_bytes = _gemm_wt_workspace(xh.device, M, k, n) if split else (0, 0)
+    check(lib().exl3_gemm_wt(xh.data_ptr(), M, k, n, wt.data_ptr(), svh.data_ptr(), y.data_ptr(), y.stride(0),
+                             dtype_code(y.dtype), ws, ws_bytes, st.word.data_ptr(), stream_ptr(xh.device)),
+          "exl3_gemm_wt")
+    st.after_launch()
+    return y
+
+
 def gemm_status(device: torch.device | None = None) -> int:
     """The prefill kernel's error word on `device` (0 = no bounded wait ever gave up); synchronises."""
     return _status(device or torch.device("cuda", torch.cuda.current_device())).read()

@@ -1,23 +1,24 @@
 """Prefill (rows > MAX_GEMV_ROWS) path of EXL3Linear (daig/omlx-exl3 src/omlx/exl3/linear.py:97-121).
 
-xh = rot(x, suh) in fp16 (the reference casts the activations to fp16 before rotating), then the fused
-tcgen05 kernel (kernels.gemm: trellis decoded into shared memory, tensor-core product, output rotation
-and svh in the epilogue). Shapes the fused kernel does not take (k % 64 != 0) decode W^T to fp16 in
-column chunks (kernels.decode_wt, bit-exact), multiply, and rotate with kernels.had_svh.
+xh = rot(x, suh) in fp16 (the reference casts the activations to fp16 before rotating), then one of two
+tcgen05 paths of this package, both with the output rotation and svh in the GEMM's epilogue:
+
+- fused (kernels.gemm): the trellis is decoded into shared memory inside the GEMM. Each weight is
+  decoded once per row tile, so it wins while the rows fit one or two tiles;
+- decode-once (kernels.decode_wt + kernels.gemm_wt): W^T is decoded to fp16 once per column chunk, then
+  multiplied by the pair-of-SMs GEMM that loads both operands with TMA. Above a few hundred rows the
+  product is tensor-core bound and the decode cost is amortised over all rows.
 """
 from __future__ import annotations
 
 import torch
 
-from .kernels import decode_wt, gemm, had_svh, rot
+from .kernels import decode_wt, gemm, gemm_wt, rot
 
-PREFILL_COL_CHUNK = 16384
-# Up to this many rows (one 256-row tile: every weight decoded once) the fused kernel is used. Up to
-# FUSED_WIDE_ROWS it is used too when the output has at least FUSED_WIDE_BLOCKS 128-column blocks: it
-# then runs 512-row tiles (every weight still decoded once) on about one CTA per SM. Beyond that, or
-# for narrower outputs (too few CTAs without a k split), decoding W once to fp16 plus a library GEMM
-# is faster on B200 at the 27B-class shapes (measured: M=512, 5120->17408: fused 793 TFLOP/s against
-# 617; 17408->5120: 414 against 667; M=4096: 892 / 790 against 1086 / 1268).
+PREFILL_COL_CHUNK = 16384          # decoded columns per chunk: bounds the fp16 W^T scratch to 32 KB per k
+# The fused kernel runs up to FUSED_MAX_ROWS rows (one 256-row tile: every weight decoded once), and up
+# to FUSED_WIDE_ROWS rows when the output has at least FUSED_WIDE_BLOCKS 128-column blocks (512-row tiles
+# on about one CTA per SM, every weight still decoded once). Beyond that decode-once is used.
 FUSED_MAX_ROWS = 256
 FUSED_WIDE_ROWS = 512
 FUSED_WIDE_BLOCKS = 128
@@ -34,11 +35,12 @@ def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, c
     xh = rot(x2, suh.reshape(1, -1))[0]
     if fused is None:
         fused = use_fused(rows, n)
-    if fused and k % 64 == 0 and n % 128 == 0:
+    if fused:
         return gemm(xh, tr, k, n, K, cb, svh, out_dtype)
-    y = torch.empty((rows, n), dtype=torch.float16, device=x2.device)
+    svh = svh.reshape(-1)
+    y = torch.empty((rows, n), dtype=out_dtype, device=x2.device)
     for c0 in range(0, n, PREFILL_COL_CHUNK):
         c = min(PREFILL_COL_CHUNK, n - c0)
         wt = decode_wt(tr, k, n, K, cb, nt0=c0 // 16, ntc=c // 16)
-        torch.matmul(xh, wt.t(), out=y[:, c0:c0 + c])
-    return had_svh(y, svh, out_dtype)
+        gemm_wt(xh, wt, svh[c0:c0 + c], out=y[:, c0:c0 + c])
+    return y
