@@ -170,7 +170,14 @@ EXL3_API int exl3_swiglu_rot(const void* gu, int gu_dtype, int rows, int n, cons
  * xh, trellis and y must be 16-byte aligned.
  */
 EXL3_API int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* trellis, int bits, int codebook,
-                       const void* svh, void* y, int out_dtype, uint32_t* status, void* stream);
+                       const void* svh, void* y, int out_dtype, void* workspace, size_t workspace_bytes,
+                       uint32_t* status, void* stream);
+/* Bytes of the optional exl3_gemm workspace (256-byte aligned) for an M x k x n call; 0 when the call
+ * would not split k. With it, calls whose row tiles x column blocks fill at most half of the SMs (narrow
+ * outputs) split k over several CTAs per tile; the first bytes are arrival counters that must be zero
+ * before the first call (every completed call leaves them zero). A null or smaller workspace runs
+ * unsplit. Calls that share a workspace must not overlap. */
+EXL3_API int exl3_gemm_workspace(int M, int k, int n, size_t* bytes);
 
 /*
  * Prefill GEMM on weights already decoded by exl3_decode_wt (tcgen05 pairs of SMs, both operands by TMA):

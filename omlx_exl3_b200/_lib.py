@@ -74,7 +74,8 @@ SIGNATURES = {
     "exl3_norm_rot": (_I, [_P, _P, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
     "exl3_swiglu_rot": (_I, [_P, _I, _I, _I, _P, _P, _P]),
     "exl3_had_svh": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
-    "exl3_gemm": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _P, _I, _P, _P]),
+    "exl3_gemm": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _P, _I, _P, _SZ, _P, _P]),
+    "exl3_gemm_workspace": (_I, [_I, _I, _I, ctypes.POINTER(_SZ)]),
     "exl3_gemm_wt_workspace": (_I, [_I, _I, _I, ctypes.POINTER(_SZ)]),
     "exl3_gemm_wt": (_I, [_P, _I, _I, _I, _P, _P, _P, _I, _I, _P, _SZ, _P, _P]),
     "exl3_qkv_post": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _P, _P, _I, _P, _P]),

@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "exl3_b200.h"
@@ -57,7 +58,10 @@ struct GemmParams {
     const __half* svh;
     void* y;
     uint32_t* status;
+    uint32_t* counters;      // [row tiles][column blocks] arrival tickets of the k split (zero at rest)
+    float* partials;         // [row tiles][column blocks][split][BM x 128 fp32, epilogue-thread order]
     int M, k, n, KT, NT, out_dtype;
+    int split;               // k parts (grid z); 1 = every CTA runs all of k
 };
 
 // ------------------------------------------------------------------------------ decode into B
@@ -123,7 +127,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = blockIdx.x;                                  // 128-column block
     const int m0 = blockIdx.y * BM;
-    const int nsteps = p.k / kGemmBK;
+    // this CTA's k part: k-steps [s0, s0 + nsteps)
+    const int ktot = p.k / kGemmBK;
+    const int s0 = (int)blockIdx.z * ktot / p.split;
+    const int nsteps = ((int)blockIdx.z + 1) * ktot / p.split - s0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGemmStages; ++s) {
             mbar_init(&full[s], 1);
@@ -131,6 +138,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        tmem_slot[1] = 0u;                                      // last-part flag
+        tmem_slot[2] = 0u;                                      // epilogue's timeout vote
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -157,7 +166,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 mbar_arrive_expect_tx(&full[s], kGemmABytes);
 #pragma unroll
                 for (int t = 0; t < BM / 256; ++t)                // boxes of 256 rows
-                    tma_load_2d(As + s * kGemmABytes + t * 256 * 128, &xmap, i * kGemmBK, m0 + 256 * t, &full[s]);
+                    tma_load_2d(As + s * kGemmABytes + t * 256 * 128, &xmap, (s0 + i) * kGemmBK, m0 + 256 * t,
+                                &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -201,10 +211,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         uint32_t* dring = reinterpret_cast<uint32_t*>(Bs + kGemmStages * kGemmBBytes + 256) +
                           (size_t)dw * kGemmDecDepth * kTiles * TW;
         int fstep = 0, fslot = 0, cslot = 0;
+        // the warp's tiles of this part's first k-step; one k-step further is kGemmBK / 16 tile rows
+        const uint32_t* tsrc =
+            p.trellis + ((size_t)(s0 * (kGemmBK / 16) + ktl) * p.NT + (size_t)nb * 8 + nt_base) * TW;
+        const size_t tstep = (size_t)(kGemmBK / 16) * p.NT * TW;
         auto fetch = [&]() {
             if (fstep < nsteps) {
-                const uint32_t* src = p.trellis +
-                                      ((size_t)(fstep * (kGemmBK / 16) + ktl) * p.NT + (size_t)nb * 8 + nt_base) * TW;
+                const uint32_t* src = tsrc + (size_t)fstep * tstep;
                 uint32_t* dst = dring + (size_t)fslot * kTiles * TW;
                 for (int c = lane; c < kTiles * TW / 4; c += 32) cp_async16(dst + c * 4, src + c * 4);
             }
@@ -259,54 +272,128 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         const int j = dw >> 2;                                  // 0..3
         const int chalf = j & 1;
         const int quarter = warp & 3;                           // TMEM lanes this warp may access
-        const bool done = mbar_wait(accum, 0);
-        if (!done) atomicOr(p.status, kStatusPipeTimeout);
+        // the accumulator wait's outcome, made uniform over the epilogue warps before any named
+        // barrier below (a wait that gave up in some threads only must not split the barriers)
+        uint32_t* vote = tmem_slot + 2;
+        if (!mbar_wait(accum, 0)) {
+            atomicOr(p.status, kStatusPipeTimeout);
+            atomicOr(vote, 1u);
+        }
+        named_bar_sync(1, 32 * kGemmDecWarps);
+        const bool done = *vote == 0u;
         tc_fence_after();
         float* xbuf = reinterpret_cast<float*>(smem);           // operand stages are free once the MMAs completed
         constexpr int kRow = 129;
+        // k split: this CTA's accumulator goes to the workspace in thread order ([pass][warp][column
+        // quad][lane] float4s: a warp's stores of one quad are 512 contiguous bytes) and the CTA takes a
+        // ticket; the last of the tile's parts sums all parts in part order and finishes.
+        const size_t tile = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+        const float4* parts = p.split > 1 ? reinterpret_cast<const float4*>(p.partials) + tile * p.split * (BM * 32)
+                                          : nullptr;
+        const size_t my_slot = (size_t)dw * 16 * 32 + lane;    // + pass * 16 warps * 16 quads * 32 lanes
+        bool finish = done;
+        if (p.split > 1 && done) {
+            float4* mine = const_cast<float4*>(parts) + (size_t)blockIdx.z * (BM * 32) + my_slot;
 #pragma unroll 1
-        for (int pass = 0; pass < TL::NH / 2; ++pass) {
-            const int h = 2 * pass + (j >> 1);
-            const int rpass = (j >> 1) * 128 + quarter * 32 + lane;     // row inside this pass's 256
-            const int row = m0 + h * 128 + quarter * 32 + lane;
-            float v[64];
-            const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN + chalf * 64);
+            for (int pass = 0; pass < TL::NH / 2; ++pass) {
+                const int h = 2 * pass + (j >> 1);
+                const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN + chalf * 64);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float part[32];
-                tc_ld32(tbase + c * 32, part);
-                tc_wait_ld();
+                for (int c = 0; c < 2; ++c) {
+                    float part[32];
+                    tc_ld32(tbase + c * 32, part);
+                    tc_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[c * 32 + i] = part[i];
-            }
-            // FWHT stages h = 1..32 stay inside a 64-column half
-#pragma unroll
-            for (int hs = 1; hs < 64; hs <<= 1) {
-#pragma unroll
-                for (int b = 0; b < 32; ++b) {
-                    const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
-                    const float a0 = v[i0], a1 = v[i1];
-                    v[i0] = a0 + a1;
-                    v[i1] = a0 - a1;
+                    for (int q4 = 0; q4 < 8; ++q4)
+                        __stcg(mine + (size_t)pass * (16 * 16 * 32) + (size_t)(8 * c + q4) * 32,
+                               make_float4(part[4 * q4], part[4 * q4 + 1], part[4 * q4 + 2], part[4 * q4 + 3]));
                 }
             }
-            // stage h = 64 pairs column c with c + 64: exchange halves through shared memory, rows
-            // padded to 129 floats
-            if (pass > 0) named_bar_sync(1, 32 * kGemmDecWarps);     // the previous pass's reads are done
-#pragma unroll
-            for (int i = 0; i < 64; ++i) xbuf[rpass * kRow + chalf * 64 + i] = v[i];
+            __threadfence();                                    // this thread's partial before the ticket
             named_bar_sync(1, 32 * kGemmDecWarps);
-#pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const float other = xbuf[rpass * kRow + (chalf ^ 1) * 64 + i];
-                v[i] = chalf == 0 ? v[i] + other : other - v[i];
+            uint32_t* flag = tmem_slot + 1;
+            if (dw == 0 && lane == 0) {
+                const uint32_t ticket = atomicAdd(p.counters + tile, 1u);
+                const bool last = ticket == (uint32_t)p.split - 1;
+                if (last) {
+                    p.counters[tile] = 0u;                      // zero at rest for the next call
+                    __threadfence();
+                }
+                *flag = last ? 1u : 0u;
             }
-            if (done && row < p.M) {
-                const __half* sv = p.svh + (size_t)nb * kGemmBN + chalf * 64;
-                const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN + chalf * 64;
-                if (p.out_dtype == EXL3_F16) store_row64(static_cast<__half*>(p.y) + off, v, sv);
-                else if (p.out_dtype == EXL3_BF16) store_row64(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
-                else store_row64(static_cast<float*>(p.y) + off, v, sv);
+            named_bar_sync(1, 32 * kGemmDecWarps);
+            finish = *flag != 0u;
+        }
+        if (finish) {
+#pragma unroll 1
+            for (int pass = 0; pass < TL::NH / 2; ++pass) {
+                const int h = 2 * pass + (j >> 1);
+                const int rpass = (j >> 1) * 128 + quarter * 32 + lane;     // row inside this pass's 256
+                const int row = m0 + h * 128 + quarter * 32 + lane;
+                float v[64];
+                if (p.split == 1) {
+                    const uint32_t tbase =
+                        tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * kGemmBN + chalf * 64);
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        float part[32];
+                        tc_ld32(tbase + c * 32, part);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[c * 32 + i] = part[i];
+                    }
+                } else {
+                    const float4* src = parts + my_slot + (size_t)pass * (16 * 16 * 32);
+#pragma unroll
+                    for (int q4 = 0; q4 < 16; ++q4) {
+                        const float4 w = __ldcg(src + (size_t)q4 * 32);
+                        v[4 * q4] = w.x;
+                        v[4 * q4 + 1] = w.y;
+                        v[4 * q4 + 2] = w.z;
+                        v[4 * q4 + 3] = w.w;
+                    }
+#pragma unroll 1
+                    for (int z = 1; z < p.split; ++z) {
+                        const float4* sz = src + (size_t)z * (BM * 32);
+#pragma unroll
+                        for (int q4 = 0; q4 < 16; ++q4) {
+                            const float4 w = __ldcg(sz + (size_t)q4 * 32);
+                            v[4 * q4] += w.x;
+                            v[4 * q4 + 1] += w.y;
+                            v[4 * q4 + 2] += w.z;
+                            v[4 * q4 + 3] += w.w;
+                        }
+                    }
+                }
+                // FWHT stages h = 1..32 stay inside a 64-column half
+#pragma unroll
+                for (int hs = 1; hs < 64; hs <<= 1) {
+#pragma unroll
+                    for (int b = 0; b < 32; ++b) {
+                        const int i0 = (b / hs) * (2 * hs) + (b % hs), i1 = i0 + hs;
+                        const float a0 = v[i0], a1 = v[i1];
+                        v[i0] = a0 + a1;
+                        v[i1] = a0 - a1;
+                    }
+                }
+                // stage h = 64 pairs column c with c + 64: exchange halves through shared memory, rows
+                // padded to 129 floats
+                if (pass > 0) named_bar_sync(1, 32 * kGemmDecWarps);     // the previous pass's reads are done
+#pragma unroll
+                for (int i = 0; i < 64; ++i) xbuf[rpass * kRow + chalf * 64 + i] = v[i];
+                named_bar_sync(1, 32 * kGemmDecWarps);
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const float other = xbuf[rpass * kRow + (chalf ^ 1) * 64 + i];
+                    v[i] = chalf == 0 ? v[i] + other : other - v[i];
+                }
+                if (row < p.M) {
+                    const __half* sv = p.svh + (size_t)nb * kGemmBN + chalf * 64;
+                    const size_t off = (size_t)row * p.n + (size_t)nb * kGemmBN + chalf * 64;
+                    if (p.out_dtype == EXL3_F16) store_row64(static_cast<__half*>(p.y) + off, v, sv);
+                    else if (p.out_dtype == EXL3_BF16) store_row64(static_cast<__nv_bfloat16*>(p.y) + off, v, sv);
+                    else store_row64(static_cast<float*>(p.y) + off, v, sv);
+                }
             }
         }
     }
@@ -320,8 +407,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 }
 
 // ------------------------------------------------------------------------------ host
+// Grid of one call: BM-row tiles x 128-column blocks x `split` k parts.
+//   - Without a split: 512-row tiles once a second 256-row tile would be needed (each weight decoded
+//     once per 512 rows), as long as they still give about one CTA per SM; else 256-row tiles.
+//   - When the tiles fill at most half of the SMs (narrow outputs: 17408 -> 5120 has 40 column
+//     blocks) and a workspace is given, k is split so that tiles x parts still fit one CTA per SM
+//     (at least 16 k-steps per part), with 512-row tiles above 256 rows so every weight is decoded
+//     once. The parts' fp32 partials go through the workspace and the last part of each tile sums
+//     them in part order.
+struct GemmPlan {
+    int bm, m_tiles, split;
+};
+
+static GemmPlan plan_gemm(int M, int k, int n, bool may_split)
+{
+    const int sms = device_sm_count(), nb = n / kGemmBN, ktot = k / kGemmBK;
+    GemmPlan pl{};
+    const long long ctas512 = (long long)nb * ((M + 511) / 512);
+    pl.bm = (M > 256 && ctas512 * 8 >= (long long)sms * 7) ? 512 : 256;
+    pl.m_tiles = (M + pl.bm - 1) / pl.bm;
+    pl.split = 1;
+    if (may_split) {
+        const int bm = M > 256 ? 512 : 256;
+        const int tiles = nb * ((M + bm - 1) / bm);
+        if (2 * tiles <= sms) {
+            const int s = std::min(std::min(8, sms / tiles), ktot / 16);
+            if (s > 1) {
+                pl.bm = bm;
+                pl.m_tiles = (M + bm - 1) / bm;
+                pl.split = s;
+            }
+        }
+    }
+    return pl;
+}
+
+// [counters: one per tile, rounded up to 256 bytes][partials: tiles x split x BM x 128 fp32]
+static size_t gemm_counter_bytes(const GemmPlan& pl, int n)
+{
+    return ((size_t)pl.m_tiles * (n / kGemmBN) * 4 + 255) / 256 * 256;
+}
+
+static size_t gemm_workspace_bytes(const GemmPlan& pl, int n)
+{
+    if (pl.split == 1) return 0;
+    return gemm_counter_bytes(pl, n) + (size_t)pl.m_tiles * (n / kGemmBN) * pl.split * pl.bm * kGemmBN * 4;
+}
+
 template <int K, int CB, int BM>
-static int launch_gemm_bm(const CUtensorMap& map, const GemmParams& prm, cudaStream_t s)
+static int launch_gemm_bm(const CUtensorMap& map, const GemmParams& prm, int m_tiles, cudaStream_t s)
 {
     constexpr int SMEM = GemmTile<BM>::SMEM;
     static bool attr_set[64] = {false};
@@ -332,36 +466,43 @@ static int launch_gemm_bm(const CUtensorMap& map, const GemmParams& prm, cudaStr
             return EXL3_E_CUDA;
         attr_set[dev] = true;
     }
-    const dim3 grid(prm.n / kGemmBN, (prm.M + BM - 1) / BM);
+    const dim3 grid(prm.n / kGemmBN, m_tiles, prm.split);
     gemm_kernel<K, CB, BM><<<grid, kGemmThreads, SMEM, s>>>(map, prm);
     return launch_status();
 }
 
-// 512-row tiles once a second 256-row tile would be needed (each weight decoded once per 512 rows),
-// as long as they still give about one CTA per SM; else 256-row tiles (more CTAs, each weight decoded
-// once per 256 rows)
 template <int K, int CB>
-static int launch_gemm_k(const CUtensorMap& map, const GemmParams& prm, cudaStream_t s)
+static int launch_gemm_k(const CUtensorMap& map, const GemmParams& prm, const GemmPlan& pl, cudaStream_t s)
 {
-    const long long ctas512 = (long long)(prm.n / kGemmBN) * ((prm.M + 511) / 512);
-    const bool tall = prm.M > 256 && ctas512 * 8 >= (long long)device_sm_count() * 7;
-    return tall ? launch_gemm_bm<K, CB, 512>(map, prm, s) : launch_gemm_bm<K, CB, 256>(map, prm, s);
+    return pl.bm == 512 ? launch_gemm_bm<K, CB, 512>(map, prm, pl.m_tiles, s)
+                        : launch_gemm_bm<K, CB, 256>(map, prm, pl.m_tiles, s);
 }
 
 template <int K>
-static int launch_gemm_cb(int cb, const CUtensorMap& map, const GemmParams& prm, cudaStream_t s)
+static int launch_gemm_cb(int cb, const CUtensorMap& map, const GemmParams& prm, const GemmPlan& pl, cudaStream_t s)
 {
     switch (cb) {
-    case 0: return launch_gemm_k<K, 0>(map, prm, s);
-    case 1: return launch_gemm_k<K, 1>(map, prm, s);
-    default: return launch_gemm_k<K, 2>(map, prm, s);
+    case 0: return launch_gemm_k<K, 0>(map, prm, pl, s);
+    case 1: return launch_gemm_k<K, 1>(map, prm, pl, s);
+    default: return launch_gemm_k<K, 2>(map, prm, pl, s);
     }
 }
 
 }  // namespace exl3
 
+extern "C" int exl3_gemm_workspace(int M, int k, int n, size_t* bytes)
+{
+    using namespace exl3;
+    if (!bytes) return EXL3_E_NULL;
+    if (M < 1 || k <= 0 || n <= 0 || k % kGemmBK || n % kGemmBN) return EXL3_E_SHAPE;
+    if (int e = check_device()) return e;
+    *bytes = gemm_workspace_bytes(plan_gemm(M, k, n, true), n);
+    return EXL3_OK;
+}
+
 extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* trellis, int bits, int codebook,
-                         const void* svh, void* y, int out_dtype, uint32_t* status, void* stream)
+                         const void* svh, void* y, int out_dtype, void* workspace, size_t workspace_bytes,
+                         uint32_t* status, void* stream)
 {
     using namespace exl3;
     if (!xh || !trellis || !svh || !y || !status) return EXL3_E_NULL;
@@ -369,9 +510,12 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
     if (bits < 1 || bits > 8) return EXL3_E_BITS;
     if (codebook < 0 || codebook > 2) return EXL3_E_CODEBOOK;
     if (out_dtype != EXL3_F16 && out_dtype != EXL3_BF16 && out_dtype != EXL3_F32) return EXL3_E_DTYPE;
-    if (!aligned(xh, 16) || !aligned(trellis, 16) || !aligned(y, 16) || !aligned(svh, 2) || !aligned(status, 4))
+    if (!aligned(xh, 16) || !aligned(trellis, 16) || !aligned(y, 16) || !aligned(svh, 2) || !aligned(status, 4) ||
+        !aligned(workspace, 256))
         return EXL3_E_ALIGN;
     if (int e = check_device()) return e;
+    GemmPlan pl = plan_gemm(M, k, n, workspace != nullptr);
+    if (pl.split > 1 && workspace_bytes < gemm_workspace_bytes(pl, n)) pl = plan_gemm(M, k, n, false);
     auto encode = exl3_get_tensormap_encoder();
     if (!encode) return EXL3_E_CUDA;
 
@@ -398,15 +542,20 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
     prm.KT = k / 16;
     prm.NT = n / 16;
     prm.out_dtype = out_dtype;
+    prm.split = pl.split;
+    if (pl.split > 1) {
+        prm.counters = static_cast<uint32_t*>(workspace);
+        prm.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gemm_counter_bytes(pl, n));
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (bits) {
-    case 1: return launch_gemm_cb<1>(codebook, map, prm, s);
-    case 2: return launch_gemm_cb<2>(codebook, map, prm, s);
-    case 3: return launch_gemm_cb<3>(codebook, map, prm, s);
-    case 4: return launch_gemm_cb<4>(codebook, map, prm, s);
-    case 5: return launch_gemm_cb<5>(codebook, map, prm, s);
-    case 6: return launch_gemm_cb<6>(codebook, map, prm, s);
-    case 7: return launch_gemm_cb<7>(codebook, map, prm, s);
-    default: return launch_gemm_cb<8>(codebook, map, prm, s);
+    case 1: return launch_gemm_cb<1>(codebook, map, prm, pl, s);
+    case 2: return launch_gemm_cb<2>(codebook, map, prm, pl, s);
+    case 3: return launch_gemm_cb<3>(codebook, map, prm, pl, s);
+    case 4: return launch_gemm_cb<4>(codebook, map, prm, pl, s);
+    case 5: return launch_gemm_cb<5>(codebook, map, prm, pl, s);
+    case 6: return launch_gemm_cb<6>(codebook, map, prm, pl, s);
+    case 7: return launch_gemm_cb<7>(codebook, map, prm, pl, s);
+    default: return launch_gemm_cb<8>(codebook, map, prm, pl, s);
     }
 }

@@ -431,10 +431,12 @@ def _status(device: torch.device) -> _StatusWord:
 
 
 def gemm(xh: torch.Tensor, trellis_u32: torch.Tensor, k: int, n: int, K: int, cb: int, svh: torch.Tensor,
-         out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None) -> torch.Tensor:
+         out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None, split: bool = True) -> torch.Tensor:
     """Prefill product with the trellis decoded in the kernel: out_dtype(had128(xh @ W) / sqrt(128) * svh)
     for xh fp16 (M, k). Needs k % 64 == 0 and n % 128 == 0 (EXL3Linear._prefill, linear.py:97-105).
-    Raises RuntimeError once an earlier launch on this device reported a timed-out wait."""
+    With `split`, narrow outputs may split k over several CTAs per tile, summed in a fixed part order (a
+    per-device workspace: calls on one device must not run concurrently on several streams). Raises
+    RuntimeError once an earlier launch on this device reported a timed-out wait."""
     M = xh.shape[0]
     _need_cuda(xh, trellis_u32, svh)
     if xh.dtype != torch.float16:
@@ -447,27 +449,30 @@ def gemm(xh: torch.Tensor, trellis_u32: torch.Tensor, k: int, n: int, K: int, cb
     xh = xh.contiguous()
     svh = svh.to(torch.float16).reshape(-1).contiguous()
     y = out if out is not None else torch.empty((M, n), dtype=out_dtype, device=xh.device)
+    ws, ws_bytes = _workspace(xh.device, "exl3_gemm_workspace", M, k, n) if split else (0, 0)
     check(lib().exl3_gemm(xh.data_ptr(), M, k, n, trellis_u32.data_ptr(), K, cb, svh.data_ptr(), y.data_ptr(),
-                          dtype_code(y.dtype), st.word.data_ptr(), stream_ptr(xh.device)), "exl3_gemm")
+                          dtype_code(y.dtype), ws, ws_bytes, st.word.data_ptr(), stream_ptr(xh.device)), "exl3_gemm")
     st.after_launch()
     return y
 
 
-_wt_workspaces: dict = {}
+_split_workspaces: dict = {}
 
 
-def _gemm_wt_workspace(device: torch.device, M: int, k: int, n: int) -> tuple[int, int]:
-    """(pointer, bytes) of this device's k-split workspace for an M x k x n call, grown on demand; new
-    buffers are zeroed (the arrival counters must be zero at rest). (0, 0) when the call runs unsplit."""
+def _workspace(device: torch.device, query: str, M: int, k: int, n: int) -> tuple[int, int]:
+    """(pointer, bytes) of this device's k-split workspace of one prefill kernel (`query` names its size
+    query) for an M x k x n call, grown on demand. Each kernel has its own buffer: the kernels place
+    their arrival counters and partials differently, and the counters must stay zero at rest (new
+    buffers are zeroed; every completed call leaves them zero). (0, 0) when the call runs unsplit."""
     need = ctypes.c_size_t()
-    check(lib().exl3_gemm_wt_workspace(M, k, n, ctypes.byref(need)), "exl3_gemm_wt_workspace")
+    check(getattr(lib(), query)(M, k, n, ctypes.byref(need)), query)
     if need.value == 0:
         return 0, 0
-    key = torch.device(device)
-    buf = _wt_workspaces.get(key)
+    key = (torch.device(device), query)
+    buf = _split_workspaces.get(key)
     if buf is None or buf.numel() < need.value:
-        buf = torch.zeros(need.value, dtype=torch.uint8, device=key)
-        _wt_workspaces[key] = buf
+        buf = torch.zeros(need.value, dtype=torch.uint8, device=key[0])
+        _split_workspaces[key] = buf
     return buf.data_ptr(), buf.numel()
 
 
@@ -493,7 +498,7 @@ def gemm_wt(xh: torch.Tensor, wt: torch.Tensor, svh: torch.Tensor, out_dtype: to
     y = out if out is not None else torch.empty((M, n), dtype=out_dtype, device=xh.device)
     if y.shape != (M, n) or y.stride(1) != 1:
         raise ValueError("out must be (M, n) with unit column stride")
-    ws, ws_bytes = _gemm_wt_workspace(xh.device, M, k, n) if split else (0, 0)
+    ws, ws_bytes = _workspace(xh.device, "exl3_gemm_wt_workspace", M, k, n) if split else (0, 0)
     check(lib().exl3_gemm_wt(xh.data_ptr(), M, k, n, wt.data_ptr(), svh.data_ptr(), y.data_ptr(), y.stride(0),
                              dtype_code(y.dtype), ws, ws_bytes, st.word.data_ptr(), stream_ptr(xh.device)),
           "exl3_gemm_wt")

@@ -16,16 +16,16 @@ import torch
 from .kernels import decode_wt, gemm, gemm_wt, rot
 
 PREFILL_COL_CHUNK = 16384          # decoded columns per chunk: bounds the fp16 W^T scratch to 32 KB per k
-# The fused kernel runs up to FUSED_MAX_ROWS rows (one 256-row tile: every weight decoded once), and up
-# to FUSED_WIDE_ROWS rows when the output has at least FUSED_WIDE_BLOCKS 128-column blocks (512-row tiles
-# on about one CTA per SM, every weight still decoded once). Beyond that decode-once is used.
-FUSED_MAX_ROWS = 256
-FUSED_WIDE_ROWS = 512
-FUSED_WIDE_BLOCKS = 128
+# Up to FUSED_MAX_ROWS rows the fused kernel decodes each weight once (256- or 512-row tiles; narrow
+# outputs split k over more CTAs) and beats decoding W^T to HBM first; above it the decode cost is
+# amortised and decode-once + the SM-pair GEMM is faster. Measured at the 27B-class shapes, 6 bpw,
+# TFLOP/s fused / decode-once: M=512 5120->17408 776 / 601, 17408->5120 660 / 542; M=4096 893 / 1241,
+# 739 / 1241.
+FUSED_MAX_ROWS = 512
 
 
 def use_fused(rows: int, n: int) -> bool:
-    return rows <= FUSED_MAX_ROWS or (rows <= FUSED_WIDE_ROWS and n // 128 >= FUSED_WIDE_BLOCKS)
+    return rows <= FUSED_MAX_ROWS
 
 
 def linear_prefill(x2: torch.Tensor, tr: torch.Tensor, k: int, n: int, K: int, cb: int, suh: torch.Tensor,

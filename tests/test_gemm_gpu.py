@@ -78,3 +78,45 @@ def test_gemm_rejects_bad_shapes(cuda):
     with pytest.raises(ValueError):
         kernels.gemm(torch.zeros((4, 96), dtype=torch.float16, device=cuda), t, 96, 128, 4, 0,
                      torch.ones(128, dtype=torch.float16, device=cuda))
+
+
+def test_gemm_k_split_deterministic(cuda):
+    """4 tiles over 64 k-steps: the call splits k over 4 CTAs per tile and the last arriving part sums the
+    parts in part order. Matches the oracle, the unsplit call within fp32 rounding, and itself bit for
+    bit; the arrival counters are left at zero (the second call gives the same bits)."""
+    from omlx_exl3_b200 import kernels
+    rng = np.random.default_rng(60)
+    M, k, n, K = 300, 4096, 512, 5
+    t = O.random_trellis(k, n, K, 61)
+    xh = rng.standard_normal((M, k)).astype(np.float16)
+    svh = np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float16)
+    x, tr, s = torch.from_numpy(xh).to(cuda), _t(t, cuda), torch.from_numpy(svh).to(cuda)
+    a = kernels.gemm(x, tr, k, n, K, 0, s)
+    b = kernels.gemm(x, tr, k, n, K, 0, s)
+    c = kernels.gemm(x, tr, k, n, K, 0, s, split=False)
+    torch.cuda.synchronize()
+    assert kernels.gemm_status(cuda) == 0
+    assert torch.equal(a, b)
+    assert not torch.equal(a, c)
+    assert O.max_rel(a.cpu().numpy(), c.cpu().numpy()) < 1e-5
+    assert O.max_rel(a.cpu().numpy(), O.gemv([t], k, [n], K, 0, xh[None], svh)) < 2e-3
+
+
+def test_gemm_config3_narrow_split(cuda):
+    """BASELINE config 3's narrow case (17408 -> 5120, M = 512, 6 bpw): 40 column blocks, so k is split
+    over 3 CTAs per tile. Checked on 256 columns in C, and every column against the unsplit kernel."""
+    from omlx_exl3_b200 import kernels
+    rng = np.random.default_rng(62)
+    M, k, n, K = 512, 17408, 5120, 6
+    t = O.random_trellis(k, n, K, 63)
+    xh = rng.standard_normal((M, k)).astype(np.float16)
+    svh = np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float16)
+    x, tr, s = torch.from_numpy(xh).to(cuda), _t(t, cuda), torch.from_numpy(svh).to(cuda)
+    a = kernels.gemm(x, tr, k, n, K, 0, s)
+    c = kernels.gemm(x, tr, k, n, K, 0, s, split=False)
+    torch.cuda.synchronize()
+    assert kernels.gemm_status(cuda) == 0
+    assert O.max_rel(a.cpu().numpy(), c.cpu().numpy()) < 1e-4
+    nc = 256
+    ref = O.gemv_c(t[:, : nc // 16].copy(), k, nc, K, 0, xh[:32], svh[:nc])
+    assert O.max_rel(a[:32, :nc].cpu().numpy(), ref) < 2e-3

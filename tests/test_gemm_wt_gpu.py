@@ -131,9 +131,10 @@ def test_linear_prefill_paths_match_oracle(cuda, fused):
 
 
 def test_linear_prefill_default_is_decode_once_for_tall_inputs():
+    """Fused up to 512 rows, decode-once above (the measured crossover at the 27B-class shapes)."""
     from omlx_exl3_b200.prefill import use_fused
-    assert use_fused(256, 5120) and use_fused(512, 17408)
-    assert not use_fused(512, 5120) and not use_fused(4096, 17408)
+    assert use_fused(256, 5120) and use_fused(512, 17408) and use_fused(512, 5120)
+    assert not use_fused(513, 5120) and not use_fused(4096, 17408)
 
 
 def test_gemm_wt_k_split_deterministic(cuda):
