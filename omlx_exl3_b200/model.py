@@ -527,9 +527,8 @@ class Qwen3EXL3(nn.Module):
         val, idx = argmax(local, n_valid, v0)                           # one pass over the fp16/bf16 logits
         if self.tp.size == 1:
             return idx
-        pack = torch.stack([val, idx.float()], dim=-1)                  # (rows, 2)
-        parts = [torch.empty_like(pack) for _ in range(self.tp.size)]
-        dist.all_gather(parts, pack, group=self.tp.group)
-        allp = torch.stack(parts)                                        # (tp, rows, 2)
+        pack = torch.stack([val, idx.float()], dim=-1)                  # (rows, 2); indices < 2^24 are exact
+        allp = torch.empty((self.tp.size,) + tuple(pack.shape), dtype=pack.dtype, device=pack.device)
+        dist.all_gather_into_tensor(allp, pack, group=self.tp.group)    # (tp, rows, 2), no per-rank copies
         best = allp[..., 0].argmax(dim=0)                                # (rows,)
         return allp[best, torch.arange(pack.shape[0], device=pack.device), 1].long()
