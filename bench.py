@@ -501,6 +501,27 @@ def run_sweep(args, torch, dev, peaks):
         b = sum(plans[i][4] for i in idx)
         by_rows[str(r)] = round(b / (time_graph(torch, dev, run(idx), reps) * 1e-3) / 1e9, 1)
 
+    # the same matrices read as the mcg and mul1 codebooks (same bytes, other hash constants; the
+    # reference's kernel test runs all three), rows 1 and 4, GB/s per codebook
+    by_codebook = {}
+    for cb, name in ((0, "3inst"), (1, "mcg"), (2, "mul1")):
+        cplans = []
+        for rows in (1, 4):
+            for (k, n) in SWEEP_SHAPES:
+                for K in SWEEP_BITS:
+                    tr, svh = mats[(k, n, K)]
+                    plan = TrellisGemvPlan(k, [n], K, cb, svh, rows, torch.float16)
+                    xh = torch.randn((1, rows, k), device=dev, generator=gen).to(torch.float16)
+                    y = torch.empty((rows, n), dtype=torch.float16, device=dev)
+                    cplans.append((plan, xh, tr, y, gemv_bytes(k, [n], [K], rows)))
+
+        def crun():
+            for plan, xh, tr, y, _ in cplans:
+                plan(xh, [tr], out=y)
+        t = time_graph(torch, dev, crun, reps)
+        by_codebook[name] = round(sum(c[4] for c in cplans) / (t * 1e-3) / 1e9, 1)
+        del cplans
+
     # end to end through the module: pinned host x in, host y out, EXL3Linear.forward (rotation + GEMV)
     lins = []
     for (k, n) in SWEEP_SHAPES:
@@ -540,6 +561,7 @@ def run_sweep(args, torch, dev, peaks):
     out = {"workload": "BASELINE config 2: 4 shapes x K{2,3,4,5,6,8} x rows{1,2,4,8}, 3inst, 96 launches per step",
            "GBps": round(achieved, 1), "ms_per_step": round(ms, 4), "accumulate": "fp32",
            "hbm_frac": round(achieved / peaks["hbm"], 4), "by_bits": by_bits, "by_rows": by_rows,
+           "by_codebook_rows_1_4": by_codebook,
            "e2e_GBps": round(total / (ms_e2e * 1e-3) / 1e9, 1),
            "e2e_path": "EXL3Linear.forward (rotation + GEMV) with pinned host x in and host y out",
            "e2e_h2d_bytes_per_step": moved[0], "e2e_d2h_bytes_per_step": moved[1]}

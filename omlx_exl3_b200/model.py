@@ -528,7 +528,8 @@ class Qwen3EXL3(nn.Module):
         if self.tp.size == 1:
             return idx
         pack = torch.stack([val, idx.float()], dim=-1)                  # (rows, 2); indices < 2^24 are exact
-        allp = torch.empty((self.tp.size,) + tuple(pack.shape), dtype=pack.dtype, device=pack.device)
-        dist.all_gather_into_tensor(allp, pack, group=self.tp.group)    # (tp, rows, 2), no per-rank copies
+        flat = torch.empty((self.tp.size * pack.shape[0], 2), dtype=pack.dtype, device=pack.device)
+        dist.all_gather_into_tensor(flat, pack, group=self.tp.group)    # ranks concatenated, no per-rank copies
+        allp = flat.view(self.tp.size, pack.shape[0], 2)                 # (tp, rows, 2)
         best = allp[..., 0].argmax(dim=0)                                # (rows,)
         return allp[best, torch.arange(pack.shape[0], device=pack.device), 1].long()
