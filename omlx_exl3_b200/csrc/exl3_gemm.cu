@@ -24,21 +24,16 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "exl3_b200.h"
 #include "exl3_common.cuh"
 #include "exl3_host.h"
+#include "exl3_gemm_dec.cuh"
 #include "exl3_tc.cuh"
 
 namespace exl3 {
-
-constexpr int kGemmBN = 128;                  // output columns per CTA
-constexpr int kGemmBK = 64;                   // k per pipeline stage (128 bytes of fp16: one swizzle row)
-constexpr int kGemmDecWarps = 16;
-constexpr int kGemmThreads = 32 * (2 + kGemmDecWarps);
-constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;   // 16 KB
-constexpr int kGemmDecDepth = 4;              // trellis k-steps in flight per decoder warp
 
 // BM rows per CTA: shared memory = operand stages + barriers + per decoder warp a ring of
 // kGemmDecDepth x 2 tiles x 32 K bytes (K <= 8: 256 bytes per tile)
@@ -52,59 +47,6 @@ struct GemmTile {
     static_assert(256 * 129 * 4 <= STAGES * (ABYTES + kGemmBBytes), "epilogue exchange buffer");
     static_assert(SMEM <= 227 * 1024, "shared memory");
 };
-
-struct GemmParams {
-    const uint32_t* trellis;
-    const __half* svh;
-    void* y;
-    uint32_t* status;
-    uint32_t* counters;      // [row tiles][column blocks] arrival tickets of the k split (zero at rest)
-    float* partials;         // [row tiles][column blocks][split][BM x 128 fp32, epilogue-thread order]
-    int M, k, n, KT, NT, out_dtype;
-    int split;               // k parts (grid z); 1 = every CTA runs all of k
-};
-
-// ------------------------------------------------------------------------------ decode into B
-// Byte offset of (row n, k) inside a K-major 128B-swizzled tile whose rows are 128 bytes (64 fp16):
-// 16-byte chunk index XOR (row mod 8), 8-row groups of 1024 bytes.
-__device__ __forceinline__ uint32_t sw128_offset(int n, int kbyte)
-{
-    return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((kbyte >> 4) ^ (n & 7))) << 4) + (kbyte & 15));
-}
-
-template <int CB>
-__device__ __forceinline__ uint32_t pack_weights(uint32_t sa, uint32_t sb)
-{
-    if constexpr (CB == 2) {
-        return __byte_perm(sa, sb, 0x5410);        // (w_a, w_b): the mul1 split word is (w, 0)
-    } else {
-        const uint32_t lo = __byte_perm(sa, sb, 0x5410), hi = __byte_perm(sa, sb, 0x7632);
-        const __half2 w = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
-        return *reinterpret_cast<const uint32_t*>(&w);
-    }
-}
-
-template <typename OT>
-__device__ __forceinline__ void store_row64(OT* dst, const float (&v)[64], const __half* svh)
-{
-#pragma unroll
-    for (int c = 0; c < 64; c += 8) {
-        if constexpr (sizeof(OT) == 4) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) dst[c + i] = from_f32<OT>(v[c + i] * kHadScale * __half2float(svh[c + i]));
-        } else {
-            uint32_t pk[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const OT a = from_f32<OT>(v[c + 2 * i] * kHadScale * __half2float(svh[c + 2 * i]));
-                const OT b = from_f32<OT>(v[c + 2 * i + 1] * kHadScale * __half2float(svh[c + 2 * i + 1]));
-                pk[i] = (uint32_t)(*reinterpret_cast<const uint16_t*>(&a)) |
-                        ((uint32_t)(*reinterpret_cast<const uint16_t*>(&b)) << 16);
-            }
-            *reinterpret_cast<uint4*>(dst + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        }
-    }
-}
 
 template <int K, int CB, int BM>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p)
@@ -416,17 +358,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 //     once. The parts' fp32 partials go through the workspace and the last part of each tile sums
 //     them in part order.
 struct GemmPlan {
-    int bm, m_tiles, split;
+    bool pair;      // the SM-pair kernel (exl3_gemm_pair.cu): n % 256 == 0
+    int bm;         // rows per tile: one-CTA 256 / 512; pair 256 x nacc
+    int nacc;       // pair: M=256 accumulators per pair tile
+    int m_tiles, split;
+    int units;      // CTAs per k part (each has its own arrival counter and partial)
 };
+
+// The SM-pair kernel runs only when the environment sets EXL3_GEMM_PAIR=1 (read at every call): it is
+// correct for every output width that is a multiple of 256 but measured slower than the one-CTA kernel
+// (M=512, 5120->17408: 620 against 732 TFLOP/s; M=4096: 732 against 884).
+static bool pair_enabled()
+{
+    const char* e = getenv("EXL3_GEMM_PAIR");
+    return e && e[0] == '1';
+}
 
 static GemmPlan plan_gemm(int M, int k, int n, bool may_split)
 {
     const int sms = device_sm_count(), nb = n / kGemmBN, ktot = k / kGemmBK;
     GemmPlan pl{};
+    pl.split = 1;
+    if (n % 256 == 0 && pair_enabled()) {
+        pl.pair = true;
+        pl.nacc = M > 256 ? 2 : 1;
+        pl.bm = 256 * pl.nacc;
+        pl.m_tiles = (M + pl.bm - 1) / pl.bm;
+        pl.units = pl.m_tiles * (n / 256) * 2;
+        if (may_split && 2 * pl.units <= sms) {
+            const int s = std::min(std::min(8, sms / pl.units), ktot / 16);
+            if (s > 1) pl.split = s;
+        }
+        return pl;
+    }
     const long long ctas512 = (long long)nb * ((M + 511) / 512);
     pl.bm = (M > 256 && ctas512 * 8 >= (long long)sms * 7) ? 512 : 256;
     pl.m_tiles = (M + pl.bm - 1) / pl.bm;
-    pl.split = 1;
     if (may_split) {
         const int bm = M > 256 ? 512 : 256;
         const int tiles = nb * ((M + bm - 1) / bm);
@@ -439,19 +406,19 @@ static GemmPlan plan_gemm(int M, int k, int n, bool may_split)
             }
         }
     }
+    pl.units = pl.m_tiles * nb;
     return pl;
 }
 
-// [counters: one per tile, rounded up to 256 bytes][partials: tiles x split x BM x 128 fp32]
-static size_t gemm_counter_bytes(const GemmPlan& pl, int n)
-{
-    return ((size_t)pl.m_tiles * (n / kGemmBN) * 4 + 255) / 256 * 256;
-}
+// [counters: one per CTA of a part, rounded up to 256 bytes][partials: units x split x a CTA's
+// accumulators (one-CTA: BM x 128 fp32; pair: 128 rows x 256 columns per accumulator)]
+static size_t gemm_counter_bytes(const GemmPlan& pl) { return ((size_t)pl.units * 4 + 255) / 256 * 256; }
 
-static size_t gemm_workspace_bytes(const GemmPlan& pl, int n)
+static size_t gemm_workspace_bytes(const GemmPlan& pl)
 {
     if (pl.split == 1) return 0;
-    return gemm_counter_bytes(pl, n) + (size_t)pl.m_tiles * (n / kGemmBN) * pl.split * pl.bm * kGemmBN * 4;
+    const size_t per_cta = pl.pair ? (size_t)pl.nacc * 128 * 256 : (size_t)pl.bm * kGemmBN;
+    return gemm_counter_bytes(pl) + (size_t)pl.units * pl.split * per_cta * 4;
 }
 
 template <int K, int CB, int BM>
@@ -496,7 +463,7 @@ extern "C" int exl3_gemm_workspace(int M, int k, int n, size_t* bytes)
     if (!bytes) return EXL3_E_NULL;
     if (M < 1 || k <= 0 || n <= 0 || k % kGemmBK || n % kGemmBN) return EXL3_E_SHAPE;
     if (int e = check_device()) return e;
-    *bytes = gemm_workspace_bytes(plan_gemm(M, k, n, true), n);
+    *bytes = gemm_workspace_bytes(plan_gemm(M, k, n, true));
     return EXL3_OK;
 }
 
@@ -515,16 +482,17 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
         return EXL3_E_ALIGN;
     if (int e = check_device()) return e;
     GemmPlan pl = plan_gemm(M, k, n, workspace != nullptr);
-    if (pl.split > 1 && workspace_bytes < gemm_workspace_bytes(pl, n)) pl = plan_gemm(M, k, n, false);
+    if (pl.split > 1 && workspace_bytes < gemm_workspace_bytes(pl)) pl = plan_gemm(M, k, n, false);
     auto encode = exl3_get_tensormap_encoder();
     if (!encode) return EXL3_E_CUDA;
 
-    // xh: fp16 (M, k) row-major -> 2D map {k, M}, box {64, 256} (a 512-row tile takes two), 128-byte
-    // swizzle, zero fill past M
+    // xh: fp16 (M, k) row-major -> 2D map {k, M}, 128-byte swizzle, zero fill past M; boxes of 64 k x
+    // 256 rows for the one-CTA kernel (a 512-row tile takes two), 128 rows for the pair kernel (each CTA
+    // loads its half of every 256-row accumulator)
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, 256u};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, pl.pair ? 128u : 256u};
     const cuuint32_t estr[2] = {1, 1};
     if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(xh), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -545,9 +513,10 @@ extern "C" int exl3_gemm(const void* xh, int M, int k, int n, const uint32_t* tr
     prm.split = pl.split;
     if (pl.split > 1) {
         prm.counters = static_cast<uint32_t*>(workspace);
-        prm.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gemm_counter_bytes(pl, n));
+        prm.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gemm_counter_bytes(pl));
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (pl.pair) return launch_gemm_pair(bits, codebook, pl.nacc, map, prm, pl.m_tiles, s);
     switch (bits) {
     case 1: return launch_gemm_cb<1>(codebook, map, prm, pl, s);
     case 2: return launch_gemm_cb<2>(codebook, map, prm, pl, s);

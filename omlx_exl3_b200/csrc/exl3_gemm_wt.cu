@@ -90,93 +90,6 @@ __device__ __forceinline__ WtUnit unit_of(const GemmWtParams& p, int u, int nste
     return w;
 }
 
-__device__ __forceinline__ uint32_t cluster_rank()
-{
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all()
-{
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// shared::cluster address of the same shared-memory object in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank)
-{
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_addr(p)), "r"(rank));
-    return d;
-}
-
-// TMA tile load into this CTA's shared memory whose completion is counted on a barrier of either CTA
-// of the pair (`bar` is a shared::cluster address). No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
-// Non-blocking test of a barrier phase, acquire at cluster scope (the pair's barriers are completed by
-// the other CTA's copies, commits and arrivals).
-__device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait by polling: a thread suspended in try_wait is not reliably woken by a completion that
-// comes from the other CTA of the pair, so these waits never suspend. Gives up (false) after limit_ns.
-// `nap_ns` > 0 spaces the polls of waits that are off the critical path (the epilogue waiting for a
-// whole tile of MMAs), leaving the issue slots to the producer and MMA threads.
-__device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, uint32_t nap_ns = 0,
-                                               uint64_t limit_ns = 2000000000ull)
-{
-    if (mbar_test_cluster(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (nap_ns) __nanosleep(nap_ns);
-        if (mbar_test_cluster(bar, parity)) return true;
-        if ((i & 255u) == 0u && global_ns() - t0 > limit_ns) return false;
-    }
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar)
-{
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                                uint32_t accumulate)
-{
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// Arrive on the barrier at the same shared-memory offset in both CTAs of the pair once the MMAs this
-// thread issued so far have completed.
-__device__ __forceinline__ void tc_commit_pair(uint64_t* bar)
-{
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            smem_addr(bar)),
-        "h"((uint16_t)3)
-        : "memory");
-}
-
 template <typename OT>
 __device__ __forceinline__ void store_row128(OT* dst, const float (&v)[128], const __half* svh)
 {

@@ -120,3 +120,43 @@ def test_gemm_config3_narrow_split(cuda):
     nc = 256
     ref = O.gemv_c(t[:, : nc // 16].copy(), k, nc, K, 0, xh[:32], svh[:nc])
     assert O.max_rel(a[:32, :nc].cpu().numpy(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("M", [100, 300, 600])
+def test_gemm_pair_matches_one_cta_kernel(cuda, M, monkeypatch):
+    """With EXL3_GEMM_PAIR=1, outputs whose width is a multiple of 256 run on SM pairs
+    (exl3_gemm_pair.cu); by default the one-CTA kernel runs. Both decode every weight exactly and
+    accumulate in fp32 in k order."""
+    from omlx_exl3_b200 import kernels
+    rng = np.random.default_rng(70 + M)
+    k, n, K = 1024, 512, 5
+    t = O.random_trellis(k, n, K, 71)
+    xh = rng.standard_normal((M, k)).astype(np.float16)
+    svh = np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float16)
+    x, tr, s = torch.from_numpy(xh).to(cuda), _t(t, cuda), torch.from_numpy(svh).to(cuda)
+    monkeypatch.setenv("EXL3_GEMM_PAIR", "1")
+    a = kernels.gemm(x, tr, k, n, K, 0, s, split=False)
+    monkeypatch.setenv("EXL3_GEMM_PAIR", "0")
+    b = kernels.gemm(x, tr, k, n, K, 0, s, split=False)
+    torch.cuda.synchronize()
+    assert kernels.gemm_status(cuda) == 0
+    assert O.max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
+    assert O.max_rel(a.cpu().numpy(), O.gemv([t], k, [n], K, 0, xh[None], svh)) < 2e-3
+
+
+def test_gemm_pair_k_split(cuda, monkeypatch):
+    """The pair kernel's k split (few pair tiles over a long k) against the oracle and itself."""
+    from omlx_exl3_b200 import kernels
+    monkeypatch.setenv("EXL3_GEMM_PAIR", "1")
+    rng = np.random.default_rng(80)
+    M, k, n, K = 300, 4096, 512, 4
+    t = O.random_trellis(k, n, K, 81)
+    xh = rng.standard_normal((M, k)).astype(np.float16)
+    svh = np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float16)
+    x, tr, s = torch.from_numpy(xh).to(cuda), _t(t, cuda), torch.from_numpy(svh).to(cuda)
+    a = kernels.gemm(x, tr, k, n, K, 0, s)
+    b = kernels.gemm(x, tr, k, n, K, 0, s)
+    torch.cuda.synchronize()
+    assert kernels.gemm_status(cuda) == 0
+    assert torch.equal(a, b)
+    assert O.max_rel(a.cpu().numpy(), O.gemv([t], k, [n], K, 0, xh[None], svh)) < 2e-3
