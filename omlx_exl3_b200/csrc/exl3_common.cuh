@@ -238,6 +238,18 @@ __device__ __forceinline__ void window_words(const uint32_t* tile, const LaneWin
     w[2] = v.hi;
 }
 
+// The eight split MMA words of one lane for one tile (the tile's words start at `tile`).
+template <int K, int CB>
+__device__ __forceinline__ void decode_tile(const uint32_t* tile, const LaneWindow<K>& lw, const HashRegs& hr,
+                                            uint32_t (&a)[8])
+{
+    uint32_t w[3], h[8];
+    window_words<K>(tile, lw, w);
+    hashes8<K, CB>(w, h, hr);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t], hr);
+}
+
 // ------------------------------------------------------------------------------ MMA
 // D += A(16x16 fp16, row) * B(16x8 fp16, col), fp32 accumulate.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -336,6 +348,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// The same copy to a 32-bit shared-window address.
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }

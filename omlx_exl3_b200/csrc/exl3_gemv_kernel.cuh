@@ -256,13 +256,44 @@ __device__ __forceinline__ void finish_row_peer(float (&v)[4], int lane, const f
     }
 }
 
+// Per-lane operands of the q/k/v finish for row r of block b: the row's position, the norm weights of
+// the block's member and the RoPE cos / sin at that position. The finishing warp loads them at the
+// segment end, so their two dependent round trips (position, then the table rows) overlap the
+// reduction and the cross-CTA arrival instead of following them.
+struct QkvPre {
+    long long pos;
+    float w[4];
+    float co[2], si[2];
+};
+
+template <typename T>
+__device__ __forceinline__ void qkv_preload(const GemvParams& p, int b, int r, int lane, QkvPre& q)
+{
+    const exl3_qkv_post_args& a = p.post;
+    const int m = b >= p.blk_off[2] ? 2 : (b >= p.blk_off[1] ? 1 : 0);
+    q.pos = a.pos[r];
+    if (m < 2) {
+        const T* w = static_cast<const T*>(m == 0 ? a.q_norm_w : a.k_norm_w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q.w[i] = to_f32(w[lane + 32 * i]);
+        const float* cs = a.cos_table + (size_t)q.pos * 64;
+        const float* sn = a.sin_table + (size_t)q.pos * 64;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            q.co[i] = cs[lane + 32 * i];
+            q.si[i] = sn[lane + 32 * i];
+        }
+    }
+}
+
 // The q/k/v group's finish, fused with exl3_qkv_post: block b is one head of q (member 0), k (1) or
 // v (2). The GEMV value is rounded to the model dtype T exactly as a stored y would be, then q/k get
 // the per-head RMSNorm (MLX rounding) and rotate-half RoPE and go to q_out / the k cache, v to the v
-// cache, all at this row's position.
+// cache, all at this row's position. The arithmetic is exl3_qkv_post's (head_rms, rope_half) on the
+// operands preloaded by qkv_preload.
 template <typename T>
 __device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const float (&sv)[4], const GemvParams& p, int b,
-                                           int r)
+                                           int r, const QkvPre& q)
 {
     fwht128_rows(v, lane);
 #pragma unroll
@@ -270,20 +301,29 @@ __device__ __forceinline__ void finish_qkv(float (&v)[4], int lane, const float 
     const exl3_qkv_post_args& a = p.post;
     const int m = b >= p.blk_off[2] ? 2 : (b >= p.blk_off[1] ? 1 : 0);
     const int head = b - (m == 0 ? 0 : (m == 1 ? p.blk_off[1] : p.blk_off[2]));
-    const long long pos = a.pos[r];
-    const float* cs = a.cos_table + (size_t)pos * 64;
-    const float* sn = a.sin_table + (size_t)pos * 64;
     __half* o;
-    if (m == 0) {
-        head_rms<T>(v, static_cast<const T*>(a.q_norm_w), a.eps, lane);
-        rope_half(v, cs, sn, lane);
-        o = static_cast<__half*>(a.q_out) + ((size_t)r * a.hq + head) * 128;
-    } else if (m == 1) {
-        head_rms<T>(v, static_cast<const T*>(a.k_norm_w), a.eps, lane);
-        rope_half(v, cs, sn, lane);
-        o = static_cast<__half*>(a.k_cache) + ((size_t)head * a.max_len + pos) * 128;
+    if (m < 2) {
+        // head RMSNorm (as head_rms), then rotate-half RoPE (as rope_half)
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / 128.0f + a.eps);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const T t = from_f32<T>(v[i] * inv);
+            v[i] = to_f32(from_f32<T>(q.w[i] * to_f32(t)));
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float x1 = v[i], x2 = v[i + 2];
+            v[i] = __fsub_rn(__fmul_rn(x1, q.co[i]), __fmul_rn(x2, q.si[i]));
+            v[i + 2] = __fadd_rn(__fmul_rn(x2, q.co[i]), __fmul_rn(x1, q.si[i]));
+        }
+        o = m == 0 ? static_cast<__half*>(a.q_out) + ((size_t)r * a.hq + head) * 128
+                   : static_cast<__half*>(a.k_cache) + ((size_t)head * a.max_len + q.pos) * 128;
     } else {
-        o = static_cast<__half*>(a.v_cache) + ((size_t)head * a.max_len + pos) * 128;
+        o = static_cast<__half*>(a.v_cache) + ((size_t)head * a.max_len + q.pos) * 128;
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[lane + 32 * i] = __float2half_rn(m == 2 ? v[i] : to_f32(from_f32<T>(v[i])));
@@ -348,13 +388,15 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
         fstep = (size_t)NCW * ntm * S::TW;
     };
     if (fi < n_units) fseek();
-    int fslot = 0;
+    // ring slots as 32-bit shared-window byte offsets (no generic-pointer arithmetic per copy)
+    const uint32_t wring32 = smem_addr(wring);
+    uint32_t foff = 0;                                                // byte offset of the slot to fill
     auto fetch = [&]() {
         if (fi < n_units) {
-            uint32_t* dst = wring + (size_t)fslot * S::UW;
+            const uint32_t dst = wring32 + foff;
 #pragma unroll
             for (int cidx = 0; cidx < kPerLane; ++cidx)
-                if (kChunks % 32 == 0 || cidx * 32 + lane < kChunks) cp_async16(dst + cidx * 128, fsrc + cidx * 128);
+                if (kChunks % 32 == 0 || cidx * 32 + lane < kChunks) cp_async16_s(dst + cidx * 512, fsrc + cidx * 128);
             fi += NCW;
             fkt += NCW;
             if (fkt >= KT) {
@@ -364,7 +406,7 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
             }
         }
         cp_async_commit();                                    // (possibly empty) group per unit
-        fslot = fslot + 1 == S::DEPTH ? 0 : fslot + 1;
+        foff = foff + S::UB == S::DEPTH * S::UB ? 0u : foff + S::UB;
     };
 #pragma unroll 1
     for (int d = 0; d < S::DEPTH - 1; ++d) fetch();
@@ -433,16 +475,22 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
             __syncwarp();
             const uint32_t* unit = wring - lane * 4 + (size_t)cslot * S::UW;
             cslot = cslot + 1 == S::DEPTH ? 0 : cslot + 1;
+            // Tile j + 1 is decoded before tile j's two MMAs are issued: the source order hands the
+            // scheduler the next tile's integer work to interleave with the MMAs (bit-identical,
+            // measured 1-3 % faster per launch than decode-then-MMA per tile).
+            uint32_t ac[8];
+            decode_tile<K, CB>(unit, lw, hr, ac);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                uint32_t w[3], h[8], a[8];
-                window_words<K>(unit + j * S::TW, lw, w);
-                hashes8<K, CB>(w, h, hr);
-#pragma unroll
-                for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t], hr);
+                uint32_t an[8];
+                if (j < 7) decode_tile<K, CB>(unit + (j + 1) * S::TW, lw, hr, an);
                 // even k of the tile: (g,2q) (g+8,2q) (g,2q+8) (g+8,2q+8); odd k: the +1 neighbours
-                mma16816(acc[j], a[0], a[4], a[2], a[6], be0, be1);
-                mma16816(acc[j], a[1], a[5], a[3], a[7], bo0, bo1);
+                mma16816(acc[j], ac[0], ac[4], ac[2], ac[6], be0, be1);
+                mma16816(acc[j], ac[1], ac[5], ac[3], ac[7], bo0, bo1);
+                if (j < 7) {
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) ac[t] = an[t];
+                }
             }
             __syncwarp();                             // the slot is refilled by the next fetch
         }
@@ -467,10 +515,15 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
         // after this kernel has completed.
         float sv[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t epoch = 0;
+        QkvPre qpre;
         if (cw < rows) {
 #pragma unroll
             for (int ii = 0; ii < 4; ++ii) sv[ii] = __half2float(p.svh[(size_t)b * 128 + lane + 32 * ii]);
             if constexpr (EPI == 2) epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch) + 1u;
+            if constexpr (EPI == 1) {
+                if (p.out_bf16) qkv_preload<__nv_bfloat16>(p, b, cw, lane, qpre);
+                else qkv_preload<__half>(p, b, cw, lane, qpre);
+            }
         }
         __syncthreads();
         for (int e = ctid; e < rows * 128; e += 32 * NCW) {
@@ -545,8 +598,8 @@ __device__ __forceinline__ void gemv_body(const GemvParams& p, uint8_t* smem, co
                 for (int ii = 0; ii < 4; ++ii) v[ii] = red[r * 128 + lane + 32 * ii];
                 const size_t yoff = (size_t)r * p.n_total + (size_t)b * 128;
                 if constexpr (EPI == 1) {
-                    if (p.out_bf16) finish_qkv<__nv_bfloat16>(v, lane, sv, p, b, r);
-                    else finish_qkv<__half>(v, lane, sv, p, b, r);
+                    if (p.out_bf16) finish_qkv<__nv_bfloat16>(v, lane, sv, p, b, r, qpre);
+                    else finish_qkv<__half>(v, lane, sv, p, b, r, qpre);
                 } else if constexpr (EPI == 2) {
                     if (p.out_bf16) finish_row_peer<__nv_bfloat16>(v, lane, sv, epoch, p, b, r);
                     else finish_row_peer<__half>(v, lane, sv, epoch, p, b, r);

@@ -145,6 +145,43 @@ class TrellisGemvPlan:
               "exl3_gemv_rot")
         return y
 
+    def bind_rot(self, suh: torch.Tensor, trellises: list[torch.Tensor]):
+        """rot_call with suh and the trellises fixed, for a module's eager path: returns f(x, out=None) -> y
+        that validates x and makes exactly one C call (every other argument was checked and converted
+        here, once). The callable keeps suh and the trellises alive; rebind after replacing them."""
+        suh = suh.to(torch.float16).contiguous()
+        if suh.numel() != self.nsub * self.k:
+            raise ValueError(f"suh has {suh.numel()} elements, expected {self.nsub}x{self.k}")
+        _need_cuda(suh)
+        self._check_trellises(trellises)
+        tptr = (ctypes.c_void_p * 3)(*[trellises[i if i < self.nsub else 0].data_ptr() for i in range(3)])
+        xs = self._xs()
+        fn = lib().exl3_gemv_rot
+        desc, tp = self._desc_ref, ctypes.cast(tptr, ctypes.c_void_p)
+        suh_p, svh_p = suh.data_ptr(), self.svh.data_ptr()
+        part_p, cnt_p, xs_p, xs_b = self.partials.data_ptr(), self.counters.data_ptr(), xs.data_ptr(), xs.numel() * 2
+        rows, k, n, odt, dev = self.rows, self.k, self.n, self.out_dtype, self.device
+        codes = {torch.float16: _lib.EXL3_F16, torch.bfloat16: _lib.EXL3_BF16, torch.float32: _lib.EXL3_F32}
+        keep = (suh, list(trellises), tptr, xs)
+
+        def call(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+            if x.shape != (rows, k) or not x.is_contiguous():
+                x = x.reshape(rows, k).contiguous()
+            code = codes.get(x.dtype)
+            if code is None:
+                raise TypeError(f"unsupported dtype {x.dtype}")
+            if not x.is_cuda:
+                raise ValueError("EXL3 kernels take CUDA tensors")
+            y = out if out is not None else torch.empty((rows, n), dtype=odt, device=dev)
+            st = fn(desc, x.data_ptr(), code, suh_p, tp, svh_p, y.data_ptr(), part_p, cnt_p, xs_p, xs_b,
+                    stream_ptr(dev))
+            if st:
+                check(st, "exl3_gemv_rot")
+            return y
+
+        call.keep = keep
+        return call
+
     def swiglu_call(self, gu: torch.Tensor, suh: torch.Tensor, trellises: list[torch.Tensor], peers=None,
                     slot: int = 0, out: torch.Tensor | None = None) -> torch.Tensor | None:
         """swiglu_rot(gu, suh) and the GEMV in one launch for a one-member plan (k = the MLP width):

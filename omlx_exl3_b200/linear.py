@@ -147,23 +147,31 @@ class EXL3Linear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._group is not None:
             return self._group.member_output(x, self._idx)
-        rt = self.runtime()
-        lead = x.shape[:-1]
-        x2 = x.reshape(-1, self.in_features)
-        if x2.shape[0] > MAX_GEMV_ROWS:
+        rt = self._rt if self._rt is not None else self.runtime()
+        x2 = x if x.dim() == 2 else x.reshape(-1, self.in_features)
+        rows = x2.shape[0]
+        if rows > MAX_GEMV_ROWS:
             y = prefill.linear_prefill(x2, rt.words, self.in_features, self.out_features, rt.bits, rt.codebook,
                                        rt.suh, rt.svh)
         else:
-            xh = self._take_primed(x)
+            xh = self._take_primed(x) if self._primed is not None else None
             gemv_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
             if xh is not None:
                 y = self.gemv_rotated(xh, gemv_dtype)
             else:            # one launch: the GEMV rotates its own input (exl3_gemv_rot)
-                y = self.plan(x2.shape[0], gemv_dtype).rot_call(x2, rt.suh, [rt.words])
-        y = y.to(x.dtype)
-        if "bias" in self:
-            y = y + self.bias.to(y.dtype)
-        return y.reshape(*lead, self.out_features)
+                # the launch with every argument but x bound once per (rows, dtype): the eager module
+                # call is otherwise dominated by host work (argument checks and conversions)
+                key = ("rot", rows, gemv_dtype)
+                f = rt.plans.get(key)
+                if f is None:
+                    f = rt.plans[key] = self.plan(rows, gemv_dtype).bind_rot(rt.suh, [rt.words])
+                y = f(x2)
+        if y.dtype != x.dtype:
+            y = y.to(x.dtype)
+        bias = self._buffers.get("bias")
+        if bias is not None:
+            y = y + bias.to(y.dtype)
+        return y if x.dim() == 2 else y.reshape(*x.shape[:-1], self.out_features)
 
 
 class EXL3SiblingGroup:
