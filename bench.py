@@ -58,7 +58,7 @@ KV_LEN = 4096
 # Warp instructions per 16x16 trellis tile of the GEMV kernel, per bitrate (rows = 1, 5120 -> 17408,
 # one launch each): smsp__inst_executed.sum / (k * n / 256) from an ncu capture of the current kernel.
 # Used for the instruction-issue (ALU) roofline of the sweep; a bitrate without a capture gets none.
-INST_PER_TILE: dict[int, float] = {2: 43.9, 3: 48.2, 4: 41.8, 5: 48.0, 6: 47.0, 8: 40.0}
+INST_PER_TILE: dict[int, float] = {2: 43.6, 3: 48.9, 4: 41.5, 5: 48.8, 6: 46.8, 8: 39.7}
 ISSUE_PER_SM_CYCLE = 4                 # warp instructions issued per SM per cycle (4 schedulers)
 
 

@@ -138,28 +138,31 @@ __device__ __forceinline__ uint32_t lane_state(const Window96<K>& v)
 }
 
 // ------------------------------------------------------------------------------ hashing
-// The decode is bound by instruction issue on two SM pipes: the integer ALU pipe (shifts, masks, byte
-// permutes, the codebook's and/xor) and the FMA pipe (integer multiply-adds, fp16 FMAs), each 16
-// lanes per scheduler per cycle. Per state the floor is one extraction (one or two ops), one IMAD
-// for the hash and one LOP3 for the codebook's and/xor. Two things keep it there (measured with
-// per-pipe instruction counters on B200):
+// The decode is bound by instruction issue. Per state the floor is one extraction (one or two ops),
+// one IMAD for the hash and one LOP3 for the codebook's and/xor. What keeps it there (measured with
+// per-pipe instruction counters and CUDA-event timing on B200):
 //   * the codebook constants live in registers the compiler cannot see through (HashRegs): as
 //     literals, one of them is re-materialised at every LOP3 / IMAD (one extra ALU op per weight,
 //     ~8 per tile);
-//   * every state is isolated exactly (mask, byte permute, multiply-high, funnel shift); folding the
-//     unmasked high bits into a correcting multiply-add costs more issue slots than it saves.
-__device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) { return __umulhi(a, b); }
+//   * every state is isolated exactly with integer-ALU ops (shift and mask, byte permute, funnel
+//     shift); folding the unmasked high bits into a correcting multiply-add costs more issue slots
+//     than it saves;
+//   * no extraction uses a multiply-high: moving fields to the top of the word and back with two
+//     multiplies (IMAD, IMAD.HI), or taking the top half with IMAD.HI, was measured 8-21 % slower per
+//     GEMV launch than shifts and masks (K = 2: 29.5 -> 23.3 us, K = 6: 28.0 -> 25.8 us, K = 8:
+//     24.3 -> 22.1 us at 5120 -> 17408, one row; the multiply-high also raised dispatch stalls);
+//   * with the extraction on the ALU pipe that pipe runs at ~70 % of its peak and limits issue, so a
+//     field inside one word is moved to the top by a plain multiply (IMAD on the FMA pipe, by a
+//     power of two from constant memory: as a literal the compiler would turn it into an ALU shift)
+//     and brought down by one shift: one ALU op instead of two (K = 6: 25.7 -> 23.8 us; issue slots
+//     60 -> 65 % busy).
 
-// Powers of two as constant-memory operands: a multiply by one stays an integer multiply-add on the
-// FMA pipe (as a literal the compiler would turn it into a shift on the ALU pipe).
+// Powers of two as constant-memory operands (see above).
 static __constant__ uint32_t c_pow2[17] = {1u << 0, 1u << 1, 1u << 2, 1u << 3, 1u << 4, 1u << 5, 1u << 6,
                                            1u << 7, 1u << 8, 1u << 9, 1u << 10, 1u << 11, 1u << 12, 1u << 13,
                                            1u << 14, 1u << 15, 1u << 16};
 
-// The 16-bit field at bit SH of the lane's window. A field inside one word is moved to the top of the
-// word and back down by two multiplies (IMAD, IMAD.HI), so it costs the ALU pipe nothing: the ALU pipe
-// already carries the codebook's and/xor and the cross-word funnel shifts, and this split of the
-// extraction between the two pipes measured 5 % faster than masking on the ALU pipe.
+// The 16-bit field at bit SH of the lane's window.
 template <int SH>
 __device__ __forceinline__ uint32_t state_exact(const uint32_t (&w)[3])
 {
@@ -167,11 +170,11 @@ __device__ __forceinline__ uint32_t state_exact(const uint32_t (&w)[3])
     if constexpr (o == 0) {
         return w[wi] & 0xffffu;
     } else if constexpr (o == 16) {
-        return mulhi(w[wi], c_pow2[16]);
+        return w[wi] >> 16;
     } else if constexpr (o == 8) {
         return __byte_perm(w[wi], 0u, 0x4421);
     } else if constexpr (o + 16 <= 32) {
-        return mulhi(w[wi] * c_pow2[16 - o], c_pow2[16]);
+        return (w[wi] * c_pow2[16 - o]) >> 16;
     } else {
         return __funnelshift_r(w[wi], w[wi + 1], o) & 0xffffu;
     }
@@ -202,11 +205,47 @@ __device__ __forceinline__ HashRegs hash_regs()
     return r;
 }
 
+// Fields of the lane's window that straddle word boundary 32 B (B = 1, 2).
+template <int K, int B>
+__host__ __device__ constexpr int cross_count()
+{
+    int c = 0;
+    for (int j = 0; j < 8; ++j) {
+        const int sh = (7 - j) * K;
+        if (sh < 32 * B && sh + 16 > 32 * B) ++c;
+    }
+    return c;
+}
+
+// The 16-bit field at bit O of one word (O + 16 <= 32), as in state_exact.
+template <int O>
+__device__ __forceinline__ uint32_t field_in_word(uint32_t x)
+{
+    if constexpr (O == 0) return x & 0xffffu;
+    else if constexpr (O == 8) return __byte_perm(x, 0u, 0x4421);
+    else return (x * c_pow2[16 - O]) >> 16;
+}
+
+// State at bit SH. Where two or more fields straddle the same word boundary, one funnel shift builds
+// the word that starts 16 bits below the boundary (m), and each of those fields is taken from it as an
+// in-word field (one ALU op each, plus the shared shift) instead of a funnel shift and a mask each
+// (K = 4 / 5: ~3 % per launch).
+template <int K, int SH>
+__device__ __forceinline__ uint32_t state_at(const uint32_t (&w)[3], const uint32_t (&m)[2])
+{
+    constexpr int wi = SH / 32, o = SH % 32;
+    if constexpr (o + 16 > 32 && cross_count<K, wi + 1>() >= 2) return field_in_word<o - 16>(m[wi]);
+    else return state_exact<SH>(w);
+}
+
 // The eight raw codebook hashes h_j = s_j * mul + add of a lane (s_j the state of position j).
 template <int K, int CB>
 __device__ __forceinline__ void hashes8(const uint32_t (&w)[3], uint32_t (&h)[8], const HashRegs& hr)
 {
-#define EXL3_HASH(J) h[J] = state_exact<(7 - J) * K>(w) * hr.mul + hr.add;
+    uint32_t m[2];                           // bits [16, 48) and [48, 80) of the window (unused ones drop out)
+    m[0] = __funnelshift_r(w[0], w[1], 16);
+    m[1] = __funnelshift_r(w[1], w[2], 16);
+#define EXL3_HASH(J) h[J] = state_at<K, (7 - J) * K>(w, m) * hr.mul + hr.add;
     EXL3_HASH(0) EXL3_HASH(1) EXL3_HASH(2) EXL3_HASH(3)
     EXL3_HASH(4) EXL3_HASH(5) EXL3_HASH(6) EXL3_HASH(7)
 #undef EXL3_HASH
