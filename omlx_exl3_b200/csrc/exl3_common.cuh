@@ -277,13 +277,22 @@ __device__ __forceinline__ void window_words(const uint32_t* tile, const LaneWin
     w[2] = v.hi;
 }
 
-// The eight split MMA words of one lane for one tile (the tile's words start at `tile`).
+// The eight split MMA words of one lane for one tile (the tile's words start at `tile`, 8-byte
+// aligned: the GEMV's shared-memory ring). At K = 8 the window's two newest words are the aligned
+// pair (2L, 2L + 1) of lane L, read with one 64-bit load.
 template <int K, int CB>
 __device__ __forceinline__ void decode_tile(const uint32_t* tile, const LaneWindow<K>& lw, const HashRegs& hr,
                                             uint32_t (&a)[8])
 {
     uint32_t w[3], h[8];
-    window_words<K>(tile, lw, w);
+    if constexpr (K == 8) {
+        const uint2 p = *reinterpret_cast<const uint2*>(tile + lw.idx[1]);
+        w[0] = p.y;
+        w[1] = p.x;
+        w[2] = tile[lw.idx[2]];
+    } else {
+        window_words<K>(tile, lw, w);
+    }
     hashes8<K, CB>(w, h, hr);
 #pragma unroll
     for (int t = 0; t < 8; ++t) a[t] = split_from_hash<CB>(h[t], hr);

@@ -28,24 +28,38 @@ __global__ void __launch_bounds__(256) decode_wt_kernel(const uint32_t* __restri
     const int nkt = min(kDecKC, KT - kt0);
     const LaneWindow<K> lw(lane);
 
-    for (int t = warp; t < nkt; t += 8) {
-        const uint32_t* tile = trellis + ((size_t)(kt0 + t) * NT + nt0 + ntl) * TW;
-        const Window96<K> v = load_window<K>(tile, lw);
-        __half d[8];
-        d[0] = dec1<CB>(lane_state<K, 0>(v));
-        d[1] = dec1<CB>(lane_state<K, 1>(v));
-        d[2] = dec1<CB>(lane_state<K, 2>(v));
-        d[3] = dec1<CB>(lane_state<K, 3>(v));
-        d[4] = dec1<CB>(lane_state<K, 4>(v));
-        d[5] = dec1<CB>(lane_state<K, 5>(v));
-        d[6] = dec1<CB>(lane_state<K, 6>(v));
-        d[7] = dec1<CB>(lane_state<K, 7>(v));
-        // position j -> (row g or g+8, k 2q, 2q+1, 2q+8, 2q+9): pairs are adjacent in k
-        const int col = t * 8 + q;   // word column of k 2q within this tile's 16 k
-        strip[g * kDecRowWords + col] = (uint32_t)__half_as_ushort(d[0]) | ((uint32_t)__half_as_ushort(d[1]) << 16);
-        strip[g * kDecRowWords + col + 4] = (uint32_t)__half_as_ushort(d[2]) | ((uint32_t)__half_as_ushort(d[3]) << 16);
-        strip[(g + 8) * kDecRowWords + col] = (uint32_t)__half_as_ushort(d[4]) | ((uint32_t)__half_as_ushort(d[5]) << 16);
-        strip[(g + 8) * kDecRowWords + col + 4] = (uint32_t)__half_as_ushort(d[6]) | ((uint32_t)__half_as_ushort(d[7]) << 16);
+    // The windows of all the warp's tiles are loaded before any is decoded, so their global-memory
+    // latencies overlap instead of following one another tile by tile.
+    constexpr int kTilesPerWarp = kDecKC / 8;
+    uint32_t win[kTilesPerWarp][3];
+#pragma unroll
+    for (int i = 0; i < kTilesPerWarp; ++i) {
+        const int t = warp + 8 * i;
+        if (t < nkt) window_words<K>(trellis + ((size_t)(kt0 + t) * NT + nt0 + ntl) * TW, lw, win[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kTilesPerWarp; ++i) {
+        const int t = warp + 8 * i;
+        if (t < nkt) {
+            // states as the GEMV extracts them (state_at), each decoded bit-exactly (dec1)
+            const uint32_t m[2] = {__funnelshift_r(win[i][0], win[i][1], 16), __funnelshift_r(win[i][1], win[i][2], 16)};
+            __half d[8];
+            d[0] = dec1<CB>(state_at<K, 7 * K>(win[i], m));
+            d[1] = dec1<CB>(state_at<K, 6 * K>(win[i], m));
+            d[2] = dec1<CB>(state_at<K, 5 * K>(win[i], m));
+            d[3] = dec1<CB>(state_at<K, 4 * K>(win[i], m));
+            d[4] = dec1<CB>(state_at<K, 3 * K>(win[i], m));
+            d[5] = dec1<CB>(state_at<K, 2 * K>(win[i], m));
+            d[6] = dec1<CB>(state_at<K, 1 * K>(win[i], m));
+            d[7] = dec1<CB>(state_at<K, 0>(win[i], m));
+            // position j -> (row g or g+8, k 2q, 2q+1, 2q+8, 2q+9): pairs are adjacent in k
+            const int col = t * 8 + q;   // word column of k 2q within this tile's 16 k
+            strip[g * kDecRowWords + col] = (uint32_t)__half_as_ushort(d[0]) | ((uint32_t)__half_as_ushort(d[1]) << 16);
+            strip[g * kDecRowWords + col + 4] = (uint32_t)__half_as_ushort(d[2]) | ((uint32_t)__half_as_ushort(d[3]) << 16);
+            strip[(g + 8) * kDecRowWords + col] = (uint32_t)__half_as_ushort(d[4]) | ((uint32_t)__half_as_ushort(d[5]) << 16);
+            strip[(g + 8) * kDecRowWords + col + 4] =
+                (uint32_t)__half_as_ushort(d[6]) | ((uint32_t)__half_as_ushort(d[7]) << 16);
+        }
     }
     __syncthreads();
 
