@@ -164,3 +164,42 @@ def test_legacy_packed_signs(cuda):
                            O.unpack_signs(sv))
     assert lin.codebook == 1
     assert O.max_rel(y, ref) < 1e-2
+
+
+def test_exl3linear_bound_launch(cuda):
+    """The eager module call binds its launch once per (rows, dtype): its output equals the unbound
+    rot_call's bit for bit, call after call, for 1-D / 2-D / 3-D and non-contiguous inputs; after the
+    buffers are replaced and reset_runtime() is called the new weights are used; bad inputs raise."""
+    from omlx_exl3_b200 import EXL3Linear
+    rng = np.random.default_rng(21)
+    k, n, K = 1024, 512, 6
+    t1, t2 = O.random_trellis(k, n, K, 31), O.random_trellis(k, n, K, 32)
+    suh = torch.from_numpy(np.where(rng.random(k) < 0.5, -1, 1).astype(np.float16))
+    svh = torch.from_numpy((rng.standard_normal(n) * 0.02).astype(np.float16))
+    lin = EXL3Linear(k, n, {"trellis": (t1.shape, torch.int16), "suh": ((k,), torch.float16),
+                            "svh": ((n,), torch.float16)}, device=cuda)
+    lin.load_state_dict({"trellis": torch.from_numpy(t1), "suh": suh, "svh": svh})
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    for rows in (1, 3):
+        rt = lin.runtime()
+        plan = lin.plan(rows, torch.float16)
+        for _ in range(3):
+            x = torch.randn((rows, k), device=cuda, generator=g).half()
+            ref = plan.rot_call(x, rt.suh, [rt.words]).clone()
+            assert torch.equal(lin(x), ref)
+            assert torch.equal(lin(x.reshape(1, rows, k)).reshape(rows, n), ref)
+            xt = torch.randn((k, rows), device=cuda, generator=g).half().t()       # non-contiguous
+            assert torch.equal(lin(xt), plan.rot_call(xt.contiguous(), rt.suh, [rt.words]))
+    x1 = torch.randn(k, device=cuda, generator=g).half()
+    assert lin(x1).shape == (n,)
+    before = lin(x1).clone()
+    lin.trellis.copy_(torch.from_numpy(t2).to(cuda))
+    lin.reset_runtime()
+    after = lin(x1)
+    ref = lin.plan(1, torch.float16).rot_call(x1.reshape(1, k), lin.runtime().suh, [lin.runtime().words])
+    assert torch.equal(after.reshape(1, n), ref) and not torch.equal(after, before)
+    with pytest.raises(ValueError):
+        lin(torch.zeros((1, k), dtype=torch.float16))                              # host tensor
+    with pytest.raises(TypeError):
+        lin(torch.zeros((1, k), dtype=torch.int32, device=cuda))
