@@ -866,7 +866,7 @@ def run_ours(args, torch, dist, rank, world, dev):
     if gemv:
         roof.update(achieved=gemv["achieved_GBps"], frac=round(gemv["achieved_GBps"] / peaks["hbm"], 4),
                     # DRAM (read + write) / algorithmic bytes of one ncu capture of the GEMV, per launch
-                    traffic=int(gemv["bytes_per_launch"] * 1.003), traffic_unit="bytes per launch",
+                    traffic=int(gemv["bytes_per_launch"] * 1.004), traffic_unit="bytes per launch",
                     launches=gemv["launches"], us_per_launch=gemv["us_per_launch"])
     roof["step_GBps_per_gpu"] = dec["step_GBps_per_gpu"]
     roof["step_frac"] = round(dec["step_GBps_per_gpu"] / peaks["hbm"], 4)
